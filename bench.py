@@ -1,0 +1,427 @@
+"""Benchmark of the sparse MoE down projection for decode on B200 (config 1 of the
+reference's north star): all 23 MoE layers of the decode path, batch rows B, ReLU^2
+activations with a zero fraction z, one hsd_sparse_down_decode launch per layer.
+
+One step = one decode pass over the 23 layers (23 launches, replayed from a CUDA graph)
+with one of 8 rotating seeded input sets, so consecutive steps read different rows and
+experts (8 sets x 23 layers touch ~0.8 GB of needed bytes per rotation at B = 1, far above
+the 126 MB L2; the 23 layers' weights are 8.26 GB).
+
+metric  sparse-down GB/s on NEEDED bytes (live rows x D/2 + live 64-groups x 4D + h + y, the
+        reference's byte model, bench/common.py:78-83), headline B = 1, z = 0.90.
+value   needed bytes of all ranks / the max over ranks of the device time of K steps.
+e2e     the same with the step's h / sel / gains copied from pinned host memory and y copied
+        back, inside the timed region.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Under torchrun every rank runs its own replica (the decode path does not shard at bs1).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "mlx-heimr-sparse-down_b200"))
+sys.path.insert(0, REPO)
+
+import hsd_b200  # noqa: E402
+from hsd_b200 import synth  # noqa: E402
+
+D, F, FS, E, TOPK = synth.D_REF, synth.F_REF, synth.FS_REF, synth.E_REF, synth.TOPK_REF
+N_LAYERS = 23      # MoE layers of the decode path (config 1); --layers lowers it for profiling
+N_SETS = 8
+METRIC = "sparse-down decode GB/s on needed bytes (23 MoE layers, B=1, z=0.90)"
+SWEEP_B = (1, 3, 8)
+SWEEP_Z = (0.80, 0.90, 0.95, 0.97)
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML in a thread while running."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 -- clocks are reported as unavailable
+            self.nv = None
+            self.err = str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(0.002)
+
+    def _sample(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:  # noqa: BLE001
+            pass
+
+    def __enter__(self):
+        if self.nv:
+            self._sample()
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.nv:
+            self._stop.set()
+            self.t.join()
+            self._sample()
+
+    def summary(self):
+        if not self.nv:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "nvml unavailable"}
+        s = sorted(self.samples)
+        med = s[len(s) // 2] if s else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons - {"gpu_idle"}),
+                "samples": len(s)}
+
+
+def needed_bytes(h, sel, y_bytes=2):
+    """Needed bytes of one launch: the union over the batch rows of live (expert, neuron)
+    rows x D/2 and live (expert, 64-group) pairs x 2*D*2, plus h in and y out."""
+    B = h.shape[0]
+    routed = (h[:, :TOPK * F] != 0).view(B * TOPK, F).to(torch.int32)
+    live = torch.zeros((E, F), dtype=torch.int32, device=h.device)
+    live.index_add_(0, sel.reshape(-1).long(), routed)
+    live = live > 0
+    shared = (h[:, TOPK * F:] != 0).any(0)
+    rows = int(live.sum()) + int(shared.sum())
+    groups = int(live.view(E, F // 64, 64).any(-1).sum()) + int(shared.view(-1, 64).any(-1).sum())
+    return rows * (D // 2) + groups * 2 * D * 2 + h.numel() * h.element_size() + B * D * y_bytes
+
+
+def make_layers(device, seed=1000):
+    """23 layers of routed + shared down projections, generated in the checkpoint layout
+    and permuted to neuron-major by the layout kernels."""
+    layers = []
+    for l in range(N_LAYERS):
+        gen = torch.Generator(device=device).manual_seed(seed + l)
+        w, s, b = synth.quantized_weights((E, D, F), gen, device)
+        sw, ss, sb = synth.quantized_weights((D, FS), gen, device)
+        pw, ps, pb = hsd_b200.to_neuron_major(w, s, b)
+        spw, sps, spb = hsd_b200.to_neuron_major(sw, ss, sb)
+        del w, s, b, sw, ss, sb
+        layers.append((pw, ps, pb, spw, sps, spb))
+    torch.cuda.synchronize(device)
+    return layers
+
+
+def make_inputs(B, z, device, seed):
+    """N_SETS x N_LAYERS seeded (h, sel, gains), packed per set into one contiguous byte
+    buffer so a step's inputs are one host-to-device copy in the end-to-end leg."""
+    NR = TOPK * F + FS
+    per = B * NR * 2 + B * TOPK * 4 + B * (TOPK + 1) * 4
+    per = (per + 255) // 256 * 256
+    sets = []
+    for si in range(N_SETS):
+        buf = torch.empty(N_LAYERS * per, dtype=torch.uint8, device=device)
+        views = []
+        for l in range(N_LAYERS):
+            gen = torch.Generator(device=device).manual_seed(seed * 1000003 + si * 1009 + l)
+            base = l * per
+            h = buf[base:base + B * NR * 2].view(torch.bfloat16).view(B, NR)
+            sel = buf[base + B * NR * 2: base + B * NR * 2 + B * TOPK * 4].view(torch.int32).view(B, TOPK)
+            o = base + B * NR * 2 + B * TOPK * 4
+            gains = buf[o:o + B * (TOPK + 1) * 4].view(torch.float32).view(B, TOPK + 1)
+            h.copy_(synth.relu2_activations((B, NR), z, gen, device))
+            logits = torch.randn((B, E), generator=gen, device=device)
+            s_, sc = synth.route_topk(logits, TOPK)
+            sel.copy_(s_)
+            gains[:, :TOPK].copy_(sc)
+            gains[:, TOPK] = 1.0
+            views.append((h, sel, gains))
+        sets.append((buf, views))
+    return sets
+
+
+class DecodeWorkload:
+    def __init__(self, layers, B, z, device, seed):
+        self.B, self.z, self.device = B, z, device
+        self.layers = layers
+        self.sets = make_inputs(B, z, device, seed)
+        self.ys = [torch.empty((N_LAYERS, B, D), dtype=torch.bfloat16, device=device) for _ in range(N_SETS)]
+        nb = [sum(needed_bytes(h, sel) for (h, sel, _) in views) for (_, views) in self.sets]
+        self.bytes_per_step = sum(nb) / len(nb)
+        self.graphs = None
+
+    def run_set(self, si):
+        _, views = self.sets[si]
+        y = self.ys[si]
+        for l, (h, sel, gains) in enumerate(views):
+            hsd_b200.sparse_down(h, sel, gains, *self.layers[l], F=F, FS=FS, D=D, topk=TOPK, out=y[l])
+
+    def capture(self):
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for si in range(N_SETS):        # warm every path once outside capture
+                self.run_set(si)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.graphs = []
+        for si in range(N_SETS):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.run_set(si)
+            self.graphs.append(g)
+        torch.cuda.synchronize(self.device)
+
+    def step(self, i):
+        self.graphs[i % N_SETS].replay()
+
+
+def barrier(dist_on):
+    if dist_on:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, dist_on, device):
+    if not dist_on:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed(fn, steps, warmup, device, dist_on):
+    """Device time (ms) of `steps` calls of fn(i) after `warmup` calls, CUDA events on the
+    current stream, barrier + synchronize on both sides, max over ranks."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize(device)
+    barrier(dist_on)
+    torch.cuda.synchronize(device)
+    st = torch.cuda.current_stream(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(steps):
+        fn(warmup + i)
+    e1.record(st)
+    torch.cuda.synchronize(device)
+    barrier(dist_on)
+    return max_over_ranks(e0.elapsed_time(e1), dist_on, device)
+
+
+def e2e_leg(wl, steps, warmup, device, dist_on):
+    """The same steps with each step's inputs copied from pinned host memory and every
+    layer's y copied back, inside the timed region."""
+    host_in = [buf.cpu().pin_memory() for (buf, _) in wl.sets]
+    host_out = [torch.empty(y.shape, dtype=y.dtype).pin_memory() for y in wl.ys]
+
+    def fn(i):
+        si = i % N_SETS
+        wl.sets[si][0].copy_(host_in[si], non_blocking=True)
+        wl.graphs[si].replay()
+        host_out[si].copy_(wl.ys[si], non_blocking=True)
+
+    ms = timed(fn, steps, warmup, device, dist_on)
+    h2d = host_in[0].numel()
+    d2h = host_out[0].numel() * host_out[0].element_size()
+    return ms, h2d, d2h
+
+
+def cpu_leg(layers, wl, budget_s=10.0, n_layers=4):
+    """The reference's decode algorithm (the C port in oracle/, OpenMP over all host
+    threads) on a bounded sample: the first n_layers layers, the workload's rotating input
+    sets, repeated until ~budget_s seconds. -> (GB/s on needed bytes, cores, sample)."""
+    import numpy as np
+    from oracle import cport
+    cores = os.cpu_count() or 1
+    host = []
+    for l in range(n_layers):
+        pw, ps, pb, spw, sps, spb = layers[l]
+        host.append(tuple(t.cpu().contiguous().view(torch.int32 if t.dtype == torch.int32 else torch.int16)
+                          .numpy().view(np.uint32 if t.dtype == torch.int32 else np.uint16)
+                          for t in (pw, ps, pb, spw, sps, spb)))
+    ins = []
+    for si in range(N_SETS):
+        _, views = wl.sets[si]
+        for l in range(n_layers):
+            h, sel, gains = views[l]
+            ins.append((l, h.float().cpu().numpy(), sel.cpu().numpy(), gains.cpu().numpy(),
+                        needed_bytes(h, sel)))
+    # warm-up (page in)
+    l, h, sel, gains, _ = ins[0]
+    cport.sparse_down(h, sel, gains, *host[l], F=F, FS=FS, D=D, topk=TOPK, nthreads=cores)
+    t0 = time.perf_counter()
+    nbytes, calls = 0, 0
+    while time.perf_counter() - t0 < budget_s:
+        for (l, h, sel, gains, nb) in ins:
+            cport.sparse_down(h, sel, gains, *host[l], F=F, FS=FS, D=D, topk=TOPK, nthreads=cores)
+            nbytes += nb
+            calls += 1
+    dt = time.perf_counter() - t0
+    sample = (f"layers 0-{n_layers - 1} of {N_LAYERS}, B={wl.B}, z={wl.z:.2f}, {N_SETS} rotating input sets, "
+              f"{calls} calls in {dt:.1f} s (C port of the reference kernel's algorithm, OpenMP)")
+    return nbytes / dt / 1e9, cores, sample
+
+
+def traffic_from_profile():
+    """Per-launch DRAM traffic of the decode kernel from the committed ncu summary."""
+    p = os.path.join(REPO, "profiles", "decode_sparse_down_ncu.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--layers", type=int, default=23, help="fewer layers: small profiling case only")
+    args = ap.parse_args()
+    global N_LAYERS
+    N_LAYERS = args.layers
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist_on = world > 1
+    if dist_on:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    warmup = max(3, args.warmup)
+    steps = max(1, args.steps)
+
+    if args.impl == "reference":
+        if rank != 0:
+            if dist_on:
+                import torch.distributed as dist
+                dist.destroy_process_group()
+            return
+        layers = make_layers(device)
+        wl = DecodeWorkload(layers, 1, 0.90, device, seed=1)
+        # one warm-up sample, then `steps` timed samples of ~1 s each (bounded)
+        per = max(1.0, min(10.0, 60.0 / (steps + warmup)))
+        cpu_leg(layers, wl, budget_s=min(2.0, per))
+        vals = [cpu_leg(layers, wl, budget_s=per) for _ in range(steps)]
+        v = sum(x[0] for x in vals) / len(vals)
+        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+                "steps": steps, "warmup": warmup, "ms_per_step": None, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 h, u4 weights, f32 accumulate",
+                "data": "synthetic", "config": {"workload": "config1: 23 MoE decode layers, B=1, z=0.90 (CPU sample)"},
+                "cpu_baseline": {"value": v, "unit": "GB/s", "cores": vals[0][1], "kind": "port",
+                                 "sample": vals[0][2]},
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "note": "the reference runs only on Apple silicon (MLX/Metal); this arm times the C port "
+                        "of its decode kernel's algorithm on the host cores"}
+        print(json.dumps(line), flush=True)
+        if dist_on:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    layers = make_layers(device)
+    wl = DecodeWorkload(layers, 1, 0.90, device, seed=1)
+    wl.capture()
+    with ClockSampler(device.index) as clk:
+        ms = timed(wl.step, steps, warmup, device, dist_on)
+    ms_step = ms / steps
+    total_bytes = wl.bytes_per_step * steps * world
+    value = total_bytes / (ms / 1e3) / 1e9
+    per_launch_bytes = wl.bytes_per_step / N_LAYERS
+    launch_ms = ms_step / N_LAYERS
+    achieved = per_launch_bytes / (launch_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+
+    e2e_ms, h2d, d2h = e2e_leg(wl, steps, warmup, device, dist_on)
+    e2e_value = wl.bytes_per_step * steps * world / (e2e_ms / 1e3) / 1e9
+
+    sweep = []
+    if not args.no_sweep:
+        for B in SWEEP_B:
+            for z in SWEEP_Z:
+                w2 = DecodeWorkload(layers, B, z, device, seed=7 + B)
+                w2.capture()
+                k = min(steps, 100)
+                m2 = timed(w2.step, k, 4, device, dist_on)
+                sweep.append({"B": B, "z": z, "us_per_layer": 1e3 * m2 / k / N_LAYERS,
+                              "needed_MB_per_layer": w2.bytes_per_step / N_LAYERS / 1e6,
+                              "GBps": w2.bytes_per_step * k / (m2 / 1e3) / 1e9})
+                del w2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, sample = cpu_leg(layers, wl, budget_s=args.cpu_seconds)
+        cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+
+    traffic = traffic_from_profile()
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 h, u4 weights, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "config1: 23 MoE decode layers (D=2688, F=1856, FS=3712, E=128, top-6), "
+                               "B=1, z=0.90, one launch per layer in a CUDA graph",
+                   "l2": f"{N_SETS} rotating input sets per layer (needed bytes per rotation "
+                         f"{N_SETS * wl.bytes_per_step / 1e9:.2f} GB > 126 MB L2); weights 8.26 GB",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "needed_MB_per_step": wl.bytes_per_step / 1e6},
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": steps * N_LAYERS,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                     "per_launch_bytes": per_launch_bytes, "launch_us": launch_ms * 1e3},
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+        "us_per_layer": launch_ms * 1e3,
+        "sweep": sweep,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,110 @@
+/*
+ * hsd.h -- C ABI of libhsd.so, the sm_100a (B200) implementation of the sparse MoE
+ * down-projection hot path of mlx-heimr-sparse-down.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed as
+ * `void*`; none allocates, synchronises the device or reads back to the host, so all
+ * of them are stream-ordered and can be captured in a CUDA graph. Every entry point
+ * returns an hsd_status; on failure hsd_last_error_string() (thread-local) says why.
+ * No entry point aborts the process and no kernel traps: a bad index met on the device
+ * is skipped and recorded in a per-device status word read by hsd_device_status().
+ *
+ * Layouts (affine 4-bit, group 64, the mlx-lm convention):
+ *   checkpoint  w [.., D, F/8] u32 (8 nibbles of one output row per word, low nibble
+ *               first), s / b [.., D, F/64] (bf16 or f16), W[o, i] = s*q + b
+ *   neuron-major (after hsd_to_neuron_major)
+ *               pw [.., F, D/8] u32: row i = neuron i, word w packs W[8w .. 8w+7, i]
+ *               ps / pb [.., F/64, D]
+ *
+ * Each declaration names the reference function it replaces (path:line inside the
+ * mlx-heimr-sparse-down project).
+ */
+#ifndef HSD_H
+#define HSD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes (the reference's only error channel is a Python assert,
+ * hsd/model.py:147,234,249, and MSL static_asserts, hsd/decode.py:50-51) */
+enum {
+  HSD_OK = 0,
+  HSD_ERR_SHAPE = 1,   /* a size the kernels do not support */
+  HSD_ERR_ALIGN = 2,   /* a pointer not aligned as the kernel needs */
+  HSD_ERR_DTYPE = 3,   /* an unsupported dtype code */
+  HSD_ERR_CUDA = 4,    /* a CUDA runtime call failed */
+  HSD_ERR_TIMEOUT = 5, /* a bounded device-side wait ran out */
+  HSD_ERR_NCCL = 6,    /* reserved for the expert-parallel exchange */
+  HSD_ERR_ARG = 7,     /* a null pointer or an out-of-range argument */
+  HSD_ERR_INDEX = 8    /* (device status word) an expert id outside [0, E) */
+};
+
+/* dtype codes */
+enum { HSD_F32 = 0, HSD_F16 = 1, HSD_BF16 = 2 };
+
+/* ---- library state ------------------------------------------------------------ */
+
+/* The message of the last failed call on this host thread ("" when none). */
+const char* hsd_last_error_string(void);
+
+/* ABI version of this header (bumped on any signature change). */
+int hsd_abi_version(void);
+
+/* Reads and clears the calling device's status word (HSD_OK or the first
+ * device-side error code recorded since the last read). Synchronises `stream`. */
+int hsd_device_status(int* status_out, void* stream);
+
+/* ---- layout: hsd/layout.py -------------------------------------------------- */
+
+/* hsd/layout.py:34 nibble_transpose(w):
+ *   w [lead, R, CW] u32 -> out [lead, 8*CW, R/8] u32 with out[.., c, wo] packing
+ *   W[8*wo + n, c], n = 0..7, low nibble first. Exact and self-inverse.
+ *   R must be a multiple of 8. out must not alias w. */
+int hsd_nibble_transpose(const uint32_t* w, uint32_t* out, int64_t lead, int64_t R,
+                         int64_t CW, void* stream);
+
+/* hsd/layout.py:72-73 (the scales / biases half of to_neuron_major):
+ *   in [lead, R, C] 16-bit -> out [lead, C, R] (swapaxes(-1, -2), bit-exact). */
+int hsd_swap_last2_u16(const uint16_t* in, uint16_t* out, int64_t lead, int64_t R,
+                       int64_t C, void* stream);
+
+/* ---- decode: hsd/decode.py ---------------------------------------------------- */
+
+/* hsd/decode.py:238 sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D,
+ * topk, sl, unr, nds, out_dtype, loadsc):
+ *   h     [B, topk*F + FS] (h_dtype: bf16 / f16 / f32), the ReLU^2 activations of the
+ *         selected experts then the shared expert's
+ *   sel   [B, topk] int32 routed expert ids in [0, E)
+ *   gains [B, topk+1] f32 (routing scores, then the shared expert's gain)
+ *   pw    [E, F, D/8] u32, ps / pb [E, F/64, D] (s_dtype: bf16 / f16)
+ *   spw   [FS, D/8] u32,   sps / spb [FS/64, D]
+ *   resid [B, D] (y_dtype) or NULL: when given, y = resid + down(h)
+ *   y     [B, D] (y_dtype: bf16 / f16 / f32)
+ * Reads only the weight rows of nonzero h entries and the scales / biases of 64-neuron
+ * groups with at least one nonzero entry. loadsc = 0 is the reference's benchmark-only
+ * switch (hsd/decode.py:25-27) that skips the scale / bias loads.
+ * Supported: D % 32 == 0, F % 64 == 0, FS % 64 == 0, 1 <= B <= 65535. */
+int hsd_sparse_down_decode(const void* h, int h_dtype, const int32_t* sel,
+                           const float* gains, const uint32_t* pw, const void* ps,
+                           const void* pb, int s_dtype, const uint32_t* spw,
+                           const void* sps, const void* spb, const void* resid, void* y,
+                           int y_dtype, int B, int D, int F, int FS, int topk, int E,
+                           int loadsc, void* stream);
+
+/* The active-index sets of the decode kernel (hsd/decode.py:86-101): per (token, slot),
+ * slot < topk routed and slot == topk the shared expert, the ascending indices of the
+ * nonzero h entries, compacted by the same warp-ballot routine the decode kernel runs.
+ *   live  [B, topk+1, max(F, FS)] int32 (entries past the count are left untouched)
+ *   count [B, topk+1] int32 */
+int hsd_decode_live_rows(const void* h, int h_dtype, int32_t* live, int32_t* count, int B,
+                         int F, int FS, int topk, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HSD_H */

@@ -1,0 +1,75 @@
+"""Sparse MoE down projection for decode (hsd/decode.py), on the neuron-major layout.
+
+One launch of the sm_100a kernel `sparse_down_decode_kernel` (csrc/hsd_decode.cu): it
+compacts the nonzero h entries of every (token, expert) with warp ballots, stages only the
+live rows' weight chunks and the live 64-groups' scale / bias chunks with 16-byte
+asynchronous copies, accumulates in fp32 and sums the per-expert partials through
+distributed shared memory of an 8-CTA cluster in a fixed order (deterministic, no scratch).
+"""
+import torch
+
+from . import _lib
+
+
+def sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D, topk,
+                sl=928, unr=2, nds=3, out_dtype=None, loadsc=1, resid=None, out=None):
+    """hsd/decode.py:238 -- the down projection over the live rows only.
+
+    h [B, topk*F + FS] (bf16 / f16 / f32), sel [B, topk] int32 (the routed experts),
+    gains [B, topk+1] f32 (routing scores, then the shared expert's gain, 1) -> y [B, D].
+    pw [E, F, D/8] / ps, pb [E, F/64, D]: the routed experts, neuron-major;
+    spw [FS, D/8] / sps, spb [FS/64, D]: the shared expert.
+
+    sl / unr / nds are the Metal kernel's tuning knobs; they are accepted for signature
+    parity and have no effect here. loadsc=0 skips the scale / bias loads (benchmark-only,
+    as in the reference). resid [B, D] (out dtype), when given, is added in the kernel
+    (y = resid + down(h)); out, when given, receives y.
+    """
+    del sl, unr, nds
+    what = "sparse_down"
+    _lib.require_cuda(h, sel, gains, pw, ps, pb, spw, sps, spb, resid, out, what=what)
+    if h.dim() != 2 or sel.dim() != 2 or gains.dim() != 2:
+        raise ValueError(f"{what}: h, sel, gains must be 2-D")
+    B = h.shape[0]
+    E = pw.shape[0]
+    if h.shape[1] != topk * F + FS:
+        raise ValueError(f"{what}: h has {h.shape[1]} columns, expected topk*F+FS = {topk * F + FS}")
+    if tuple(sel.shape) != (B, topk) or sel.dtype != torch.int32:
+        raise ValueError(f"{what}: sel must be int32 [{B}, {topk}] (got {sel.dtype} {tuple(sel.shape)})")
+    if tuple(gains.shape) != (B, topk + 1) or gains.dtype != torch.float32:
+        raise ValueError(f"{what}: gains must be float32 [{B}, {topk + 1}]")
+    if tuple(pw.shape) != (E, F, D // 8) or tuple(ps.shape) != (E, F // 64, D) or ps.shape != pb.shape:
+        raise ValueError(f"{what}: routed layout shapes {tuple(pw.shape)} {tuple(ps.shape)} {tuple(pb.shape)}"
+                         f" do not match E={E} F={F} D={D}")
+    if tuple(spw.shape) != (FS, D // 8) or tuple(sps.shape) != (FS // 64, D) or sps.shape != spb.shape:
+        raise ValueError(f"{what}: shared layout shapes do not match FS={FS} D={D}")
+    if ps.dtype != pb.dtype or sps.dtype != ps.dtype or spb.dtype != ps.dtype:
+        raise TypeError(f"{what}: scales and biases must share one 16-bit dtype")
+    od = out_dtype or h.dtype
+    if out is None:
+        out = torch.empty((B, D), dtype=od, device=h.device)
+    elif out.dtype != od or tuple(out.shape) != (B, D):
+        raise ValueError(f"{what}: out must be {od} [{B}, {D}]")
+    if resid is not None and (resid.dtype != od or tuple(resid.shape) != (B, D)):
+        raise ValueError(f"{what}: resid must be {od} [{B}, {D}]")
+    if B == 0:
+        return out
+    _lib.call("hsd_sparse_down_decode", _lib.ptr(h), _lib.dtype_code(h, what), _lib.ptr(sel),
+              _lib.ptr(gains), _lib.ptr(pw), _lib.ptr(ps), _lib.ptr(pb), _lib.dtype_code(ps, what),
+              _lib.ptr(spw), _lib.ptr(sps), _lib.ptr(spb), _lib.ptr(resid), _lib.ptr(out),
+              _lib.dtype_code(out, what), B, D, F, FS, topk, E, 1 if loadsc else 0, _lib.stream_of(h))
+    return out
+
+
+def live_rows(h, *, F, FS, topk):
+    """The active-index sets: per (token, slot) the ascending indices of nonzero h entries,
+    from the decode kernel's own ballot compaction.
+    -> (live [B, topk+1, max(F, FS)] int32, valid up to count; count [B, topk+1] int32)."""
+    _lib.require_cuda(h, what="live_rows")
+    B = h.shape[0]
+    live = torch.full((B, topk + 1, max(F, FS)), -1, dtype=torch.int32, device=h.device)
+    count = torch.zeros((B, topk + 1), dtype=torch.int32, device=h.device)
+    if B:
+        _lib.call("hsd_decode_live_rows", _lib.ptr(h), _lib.dtype_code(h, "live_rows"), _lib.ptr(live),
+                  _lib.ptr(count), B, F, FS, topk, _lib.stream_of(h))
+    return live, count

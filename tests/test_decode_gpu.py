@@ -1,0 +1,168 @@
+"""sparse_down on the GPU against the oracle (the reference's
+tests/test_layout_decode.py:154-185 on synthetic inputs): outputs within 2e-3 of the fp32
+dequantised reference (the north-star bar is 1e-2), the active-index sets bit-exact."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, bits16_np, f32_np, rel_err, words_np
+from oracle import cport
+from oracle import decode as od
+from oracle.quant import bf16_bits_to_f32
+
+import hsd_b200
+from hsd_b200 import synth
+
+TOL = 2e-3       # the reference test's bound on max|out - ref| / max|ref|
+
+
+def layouts(c):
+    pw, ps, pb = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"])
+    spw, sps, spb = hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
+    return pw, ps, pb, spw, sps, spb
+
+
+def oracle_y(c):
+    """The fp32 dequantised reference through the C oracle (dense path, checkpoint layout)."""
+    return cport.dense_down(f32_np(c["h"]), c["sel"].cpu().numpy(), c["gains"].cpu().numpy(),
+                            words_np(c["w"]), bits16_np(c["s"]), bits16_np(c["b"]), words_np(c["sw"]),
+                            bits16_np(c["ss"]), bits16_np(c["sb"]), F=c["F"], FS=c["FS"], D=c["D"],
+                            topk=c["topk"])
+
+
+def run(c, lay, **kw):
+    return hsd_b200.sparse_down(c["h"], c["sel"], c["gains"], *lay, F=c["F"], FS=c["FS"], D=c["D"],
+                                topk=c["topk"], **kw)
+
+
+@pytest.mark.gpu
+def test_golden_small_case(cuda):
+    g = np.load(os.path.join(GOLDEN, "decode_small.npz"))
+    D, F, FS, E, topk, B = (int(x) for x in g["dims"])
+    t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).view(dt)).to(cuda)  # noqa: E731
+    h = t(g["h"], np.int16).view(torch.bfloat16)
+    args = [t(g["pw"], np.int32), t(g["ps"], np.int16).view(torch.bfloat16), t(g["pb"], np.int16).view(torch.bfloat16),
+            t(g["spw"], np.int32), t(g["sps"], np.int16).view(torch.bfloat16), t(g["spb"], np.int16).view(torch.bfloat16)]
+    y = hsd_b200.sparse_down(h, t(g["sel"], np.int32), t(g["gains"], np.float32), *args, F=F, FS=FS, D=D,
+                             topk=topk, out_dtype=torch.float32)
+    assert rel_err(f32_np(y), g["y"]) < TOL
+    assert hsd_b200.device_status() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B", [1, 3, 4, 8])
+@pytest.mark.parametrize("z", [0.80, 0.90, 0.97])
+def test_reference_shapes_vs_fp32_dequant(cuda, B, z):
+    c = synth.decode_case(seed=100 + B, B=B, zero_frac=z, device=cuda)
+    lay = layouts(c)
+    y = run(c, lay, out_dtype=torch.float32)
+    ref = oracle_y(c)
+    err = rel_err(f32_np(y), ref)
+    assert err < TOL, err
+    ybf = run(c, lay)                               # default: h's dtype (bf16)
+    assert ybf.dtype == torch.bfloat16
+    assert rel_err(f32_np(ybf), ref) < 1e-2
+    assert hsd_b200.device_status() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dims", [
+    dict(D=256, F=128, FS=256, E=8, topk=2),
+    dict(D=96, F=64, FS=192, E=3, topk=1),        # tail output chunk (96 = 64 + 32), 3 groups per token
+    dict(D=2688, F=1856, FS=3712, E=128, topk=8),  # more slots than the cluster has CTAs
+    dict(D=512, F=8192, FS=64, E=4, topk=2),       # a CTA spans more than one 32-group batch
+])
+def test_odd_shapes(cuda, dims):
+    c = synth.decode_case(seed=3, B=2, zero_frac=0.5, device=cuda, **dims)
+    y = run(c, layouts(c), out_dtype=torch.float32)
+    assert rel_err(f32_np(y), oracle_y(c)) < TOL
+
+
+@pytest.mark.gpu
+def test_dense_rows_more_than_one_stage(cuda):
+    """No zeros at all: every row live, so a CTA stages several 512-row sub-batches."""
+    c = synth.decode_case(seed=4, B=1, zero_frac=0.001, device=cuda)
+    y = run(c, layouts(c), out_dtype=torch.float32)
+    assert rel_err(f32_np(y), oracle_y(c)) < TOL
+
+
+@pytest.mark.gpu
+def test_all_zero_h_gives_resid(cuda):
+    c = synth.decode_case(seed=5, B=2, zero_frac=0.9, device=cuda)
+    c["h"].zero_()
+    resid = torch.randn((2, c["D"]), device=cuda).to(torch.bfloat16)
+    y = run(c, layouts(c), resid=resid)
+    assert torch.equal(y, resid)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("h_dtype", [torch.float16, torch.float32])
+def test_h_dtypes_and_resid(cuda, h_dtype):
+    c = synth.decode_case(seed=6, B=3, zero_frac=0.9, device=cuda, h_dtype=h_dtype)
+    lay = layouts(c)
+    resid = torch.randn((3, c["D"]), device=cuda, dtype=torch.float32)
+    y = run(c, lay, out_dtype=torch.float32, resid=resid)
+    assert rel_err(f32_np(y - resid), oracle_y(c)) < TOL
+
+
+@pytest.mark.gpu
+def test_loadsc0_measurement_switch(cuda):
+    """loadsc=0 (benchmark-only) computes sum over live groups of sum(h q) + sum(h)."""
+    c = synth.decode_case(seed=8, B=1, D=256, F=128, FS=256, E=4, topk=2, zero_frac=0.8, device=cuda)
+    lay = layouts(c)
+    y = run(c, lay, out_dtype=torch.float32, loadsc=0)
+    ones = [torch.ones_like(x).to(x.dtype) for x in (lay[1], lay[4])]
+    zeros = [torch.zeros_like(x) for x in (lay[2], lay[5])]
+    hsum_lay = (lay[0], ones[0], ones[0], lay[3], ones[1], ones[1])
+    y1 = run(c, hsum_lay, out_dtype=torch.float32)         # s = b = 1: sum h q + sum h
+    assert rel_err(f32_np(y), f32_np(y1)) < 1e-5
+    del zeros
+
+
+@pytest.mark.gpu
+def test_deterministic(cuda):
+    c = synth.decode_case(seed=9, B=4, zero_frac=0.9, device=cuda)
+    lay = layouts(c)
+    y0 = run(c, lay, out_dtype=torch.float32)
+    for _ in range(3):
+        assert torch.equal(run(c, lay, out_dtype=torch.float32), y0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("z", [0.0, 0.9, 0.99])
+def test_active_index_sets_bit_exact(cuda, z):
+    c = synth.decode_case(seed=10, B=3, zero_frac=max(z, 1e-6), device=cuda)
+    live, count = hsd_b200.live_rows(c["h"], F=c["F"], FS=c["FS"], topk=c["topk"])
+    ref = od.live_rows(f32_np(c["h"]), F=c["F"], FS=c["FS"], topk=c["topk"])
+    live, count = live.cpu().numpy(), count.cpu().numpy()
+    for b in range(3):
+        for k in range(c["topk"] + 1):
+            n = int(count[b, k])
+            assert n == len(ref[b][k])
+            assert np.array_equal(live[b, k, :n], ref[b][k])
+
+
+@pytest.mark.gpu
+def test_invalid_expert_is_reported_not_faulted(cuda):
+    c = synth.decode_case(seed=12, B=2, D=256, F=128, FS=256, E=8, topk=2, zero_frac=0.9, device=cuda)
+    lay = layouts(c)
+    assert hsd_b200.device_status() == 0
+    c["sel"][1, 0] = 8                              # == E: out of range
+    run(c, lay, out_dtype=torch.float32)
+    assert hsd_b200.device_status() == 8            # HSD_ERR_INDEX
+    assert hsd_b200.device_status() == 0            # read clears it
+
+
+@pytest.mark.gpu
+def test_sparse_equals_live_row_oracle_order(cuda):
+    """Against the C port of the reference kernel's algebra on the neuron-major layout."""
+    c = synth.decode_case(seed=13, B=2, zero_frac=0.95, device=cuda)
+    lay = layouts(c)
+    y = run(c, lay, out_dtype=torch.float32)
+    yc = cport.sparse_down(f32_np(c["h"]), c["sel"].cpu().numpy(), c["gains"].cpu().numpy(), words_np(lay[0]),
+                           bits16_np(lay[1]), bits16_np(lay[2]), words_np(lay[3]), bits16_np(lay[4]),
+                           bits16_np(lay[5]), F=c["F"], FS=c["FS"], D=c["D"], topk=c["topk"])
+    assert rel_err(f32_np(y), yc) < TOL
+    _ = bf16_bits_to_f32

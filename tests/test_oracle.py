@@ -1,0 +1,129 @@
+"""The CPU oracle against the reference's known-answer tests and the golden fixtures,
+and its restatements against each other (no GPU)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, rel_err
+from oracle import cport
+from oracle import decode as od
+from oracle import layout as ol
+from oracle.quant import bf16_bits_to_f32, dequantize, dequantize_neuron_major
+
+
+def slow_reference_transpose(w):
+    """The reference test's slow numpy method (tests/test_layout_decode.py:38-52 of the
+    reference), restated: unpack every word to 8 nibbles column by column, move them,
+    pack them again."""
+    lead = w.shape[:-2]
+    R, CW = w.shape[-2], w.shape[-1]
+    C = CW * 8
+    nib = np.zeros((*lead, R, C), dtype=np.uint32)
+    for k in range(8):
+        nib[..., k::8] = (w >> np.uint32(4 * k)) & np.uint32(0xF)
+    t = np.swapaxes(nib, -1, -2)
+    out = np.zeros((*lead, C, R // 8), dtype=np.uint32)
+    for k in range(8):
+        out |= t[..., k::8] << np.uint32(4 * k)
+    return out
+
+
+# the reference test's shapes (tests/test_layout_decode.py:59)
+REF_SHAPES = ((5, 24, 9), (2688, 232), (1856, 336), (3712, 336), (3, 2688, 232))
+
+
+@pytest.mark.parametrize("shape", REF_SHAPES)
+def test_nibble_transpose_exact_and_self_inverse(shape):
+    rng = np.random.default_rng(0)
+    w = rng.integers(0, 2**32, size=shape, dtype=np.uint64).astype(np.uint32)
+    t = ol.nibble_transpose(w)
+    assert t.shape == (*shape[:-2], shape[-1] * 8, shape[-2] // 8)
+    assert np.array_equal(t, slow_reference_transpose(w))
+    assert np.array_equal(ol.nibble_transpose(t), w)
+
+
+@pytest.mark.parametrize("name", ["nibble_transpose_5x24x9.npz", "nibble_transpose_2x16x4.npz"])
+def test_nibble_transpose_golden(name):
+    g = np.load(os.path.join(GOLDEN, name))
+    assert np.array_equal(ol.nibble_transpose(g["w"]), g["t"])
+    assert np.array_equal(cport.nibble_transpose(g["w"]), g["t"])
+
+
+def test_c_transpose_matches_numpy():
+    rng = np.random.default_rng(1)
+    w = rng.integers(0, 2**32, size=(3, 64, 12), dtype=np.uint64).astype(np.uint32)
+    assert np.array_equal(cport.nibble_transpose(w), ol.nibble_transpose(w))
+
+
+def test_to_neuron_major_is_the_same_bytes():
+    """Dequantising the neuron-major layout gives exactly the checkpoint layout's weights
+    (the reference's tests/test_layout_decode.py:70-83, on synthetic weights)."""
+    from hsd_b200 import synth
+    gen = torch.Generator().manual_seed(3)
+    w, s, b = synth.quantized_weights((4, 128, 192), gen, "cpu")
+    w = w.numpy().view(np.uint32)
+    s = bf16_bits_to_f32(s.view(torch.int16).numpy().view(np.uint16))
+    b = bf16_bits_to_f32(b.view(torch.int16).numpy().view(np.uint16))
+    pw, ps, pb = ol.to_neuron_major(w, s, b)
+    ref = dequantize(w, s, b)                               # [E, D, F]
+    out = dequantize_neuron_major(pw, ps, pb)               # [E, F, D]
+    assert np.array_equal(np.swapaxes(out, -1, -2), ref)
+
+
+def _golden_decode():
+    g = np.load(os.path.join(GOLDEN, "decode_small.npz"))
+    D, F, FS, E, topk, B = (int(x) for x in g["dims"])
+    return g, D, F, FS, topk
+
+
+def test_decode_golden_both_restatements():
+    g, D, F, FS, topk = _golden_decode()
+    f = bf16_bits_to_f32
+    h = f(g["h"])
+    y1 = od.reference_dense(h, g["sel"], g["gains"], g["w"], f(g["s"]), f(g["b"]), g["sw"], f(g["ss"]),
+                            f(g["sb"]), F=F, FS=FS, topk=topk)
+    assert rel_err(y1, g["y"]) < 1e-6
+    y2 = od.sparse_live(h, g["sel"], g["gains"], g["pw"], f(g["ps"]), f(g["pb"]), g["spw"], f(g["sps"]),
+                        f(g["spb"]), F=F, FS=FS, topk=topk)
+    assert rel_err(y2, g["y"]) < 1e-5
+    y3 = cport.sparse_down(h, g["sel"], g["gains"], g["pw"], g["ps"], g["pb"], g["spw"], g["sps"], g["spb"],
+                           F=F, FS=FS, D=D, topk=topk)
+    assert rel_err(y3, g["y"]) < 1e-5
+    y4 = cport.dense_down(h, g["sel"], g["gains"], g["w"], g["s"], g["b"], g["sw"], g["ss"], g["sb"],
+                          F=F, FS=FS, D=D, topk=topk)
+    assert rel_err(y4, g["y"]) < 1e-5
+
+
+def test_decode_restatements_agree_reference_shapes():
+    """At the reference shapes (one token, 90 % zeros) the dense fp32 dequantised path and
+    the live-row algebra agree to fp32 summation order."""
+    from hsd_b200 import synth
+    c = synth.decode_case(seed=11, B=1, E=16, zero_frac=0.9)
+    f = bf16_bits_to_f32
+    w = c["w"].numpy().view(np.uint32)
+    s, b = (x.view(torch.int16).numpy().view(np.uint16) for x in (c["s"], c["b"]))
+    sw = c["sw"].numpy().view(np.uint32)
+    ss, sb = (x.view(torch.int16).numpy().view(np.uint16) for x in (c["ss"], c["sb"]))
+    h = c["h"].float().numpy()
+    sel, gains = c["sel"].numpy(), c["gains"].numpy()
+    kw = dict(F=c["F"], FS=c["FS"], topk=c["topk"])
+    y_ref = od.reference_dense(h, sel, gains, w, f(s), f(b), sw, f(ss), f(sb), **kw)
+    pw, ps, pb = ol.to_neuron_major(w, s, b)
+    spw, sps, spb = ol.to_neuron_major(sw, ss, sb)
+    y_c = cport.sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, D=c["D"], **kw)
+    assert rel_err(y_c, y_ref) < 1e-4
+
+
+def test_live_rows_and_byte_model():
+    h = np.zeros((2, 3 * 64 + 128), np.float32)
+    h[0, [1, 5, 64]] = 1.0
+    h[1, [1, 200, 300]] = 2.0
+    sel = np.array([[0, 1], [0, 2]], np.int32)
+    lr = od.live_rows(h, F=96, FS=128, topk=2)
+    assert list(lr[0][0]) == [1, 5, 64] and list(lr[0][1]) == [] and list(lr[1][2]) == [8, 108]
+    nb = od.needed_bytes(h, sel, F=96, FS=128, D=64, topk=2)
+    # rows: (0,1),(0,5),(0,64) for token 0 slot 0; (0,1) again for token 1 -> union 3; shared 2
+    assert nb["rows"] == 3 + 2
+    assert nb["groups"] == 2 + 2   # (0,0),(0,1) routed; (-1,0),(-1,1) shared
