@@ -6,28 +6,38 @@
 //
 // Work split (one token = one row b of h):
 //   The token's 64-neuron groups are listed slot by slot (topk routed experts, then the
-//   shared expert): GT = topk*F/64 + FS/64 groups (232 at the reference shapes). The D
-//   outputs are cut into chunks of C outputs (C/2 contiguous bytes of every neuron row).
-//   A thread-block CLUSTER of 8 CTAs owns one (token, chunk); CTA `rank` of the cluster
-//   owns groups [rank*GT/8, (rank+1)*GT/8) -- at the reference shapes exactly one routed
-//   expert or one half of the shared expert (29 groups) each. The 8 partial outputs are
-//   summed through distributed shared memory in a fixed rank order, so the result is
-//   deterministic and no scratch memory, atomics or second kernel is needed.
+//   shared expert): GT = topk*F/64 + FS/64 groups (232 at the reference shapes); they are
+//   the contiguous 64-column blocks of h's row. The D outputs are cut into chunks of C
+//   outputs (C/2 contiguous bytes of every neuron row). A thread-block CLUSTER of 8 CTAs
+//   owns one (token, chunk); CTA `rank` owns groups [rank*GT/8, (rank+1)*GT/8) -- at the
+//   reference shapes one routed expert or one half of the shared expert (29 groups). The 8
+//   partial outputs are summed through distributed shared memory in a fixed rank order:
+//   deterministic, with no scratch memory, atomics or second kernel.
 //
 // Per CTA and batch of up to 32 groups:
-//   1. each warp reads the h of its groups (64 values each) and builds the group's live
-//      mask with two warp ballots; warp 0 scans the live counts;
-//   2. the live rows are compacted (ballot prefix popcounts) into an ascending list;
-//   3. 16-byte cp.async copies stage, for live groups only, the chunk of the group's
-//      scales and biases, and for live rows only, the row's C/2-byte chunk -- all copies
-//      of a batch are in flight at once;
-//   4. thread (word wp, row lane rl) walks rows rl, rl+NRL, ... accumulating, per 64-group,
-//      acc'[n] = sum h * (1 + q_n/16) and hsum = sum h in fp32, and folds each finished group
-//      in as out[n] += g * (16*s[n]*(acc'[n] - hsum) + b[n]*hsum) -- the same affine algebra as
-//      the reference (s * sum(h q) + b * sum(h)); 1 + q/16 is built exactly from the nibble
-//      by bit operations, which spares an integer-to-float conversion per weight.
-//   5. the NRL row lanes are reduced in shared memory in a fixed order.
+//   1. one 16-byte load per thread brings the batch's h columns (and each group's expert
+//      id and gain) into shared memory;
+//   2. each warp builds its groups' live masks with two ballots and, for a live group,
+//      starts the TMA bulk copies of the group's scale and bias chunks (C*2 bytes each);
+//   3. every warp scans the live counts and compacts its groups' live rows into an
+//      ascending list (ballot prefix popcounts); each lane holding a live row starts the
+//      TMA bulk copy of that row's C/2-byte chunk. All copies of the batch complete on one
+//      mbarrier whose single arrival carries the batch's byte count, so the whole batch is
+//      in flight at once and a copy costs one instruction;
+//   4. thread (word wp, group lane gl) walks the live rows of groups gl, gl+NGL, ... in
+//      shared memory, accumulating acc'[n] = sum h * (1 + q_n/16) and hsum = sum h in fp32,
+//      and folds each group in as out[n] += g * (16*s[n]*(acc'[n] - hsum) + b[n]*hsum) --
+//      the reference's affine algebra (s * sum(h q) + b * sum(h)); 1 + q/16 is built exactly
+//      from the nibble with bit operations, sparing an integer-to-float conversion per weight;
+//   5. the NGL group lanes are reduced in shared memory in a fixed order.
+// Weights are streamed with an L2 evict-first policy (they are not reused by the step).
+// The launch uses programmatic dependent launch: the kernel releases its dependents at
+// once and waits (griddepcontrol.wait) for the previous kernel before its first read, so
+// back-to-back layers overlap launch latency with the previous layer's tail. Every
+// mbarrier wait is bounded (2 s of %globaltimer); running out sets HSD_ERR_TIMEOUT in the
+// status word, waits once more (bounded) for the copies in flight and finishes.
 #include <cooperative_groups.h>
+#include <cstdlib>
 
 #include "hsd_common.cuh"
 
@@ -37,12 +47,18 @@ HSD_DEFINE_STATUS(decode)
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
 constexpr int kCluster = 8;    // CTAs per (token, chunk)
 constexpr int kGB = 32;        // groups per batch
-constexpr int kRB = 512;       // staged rows per sub-batch
 constexpr int kGS = 64;        // quantisation group size
+
+template <int C>
+struct DecodeCfg {
+  static constexpr int NWC = C / 8;                    // words of one row in a chunk
+  static constexpr int THREADS = 512;                  // 16 full warps (ballots use full masks)
+  static constexpr int WARPS = THREADS / 32;
+  static constexpr int NGL = THREADS / NWC;            // group lanes: 32 (C = 128), 21 (C = 192)
+  static constexpr int RB = 1024;                      // staged rows per sub-batch
+};
 
 struct DecodeParams {
   const void* h;
@@ -64,13 +80,15 @@ struct DecodeParams {
 
 template <int C>
 struct DecodeSmem {
-  static constexpr int NWC = C / 8;             // words of one row in a chunk
-  float hs[kGB * kGS];                          // the batch's h values (fp32)
-  uint32_t stage[kRB * NWC];                    // staged row chunks
+  using Cfg = DecodeCfg<C>;
+  uint32_t stage[Cfg::RB * Cfg::NWC];           // staged row chunks (also the group-lane partials)
   uint16_t meta_s[kGB * C];                     // staged scale chunks (16-bit)
   uint16_t meta_b[kGB * C];                     // staged bias chunks
+  float hs[kGB * kGS];                          // the batch's h values (fp32)
+  float hrow[kGB * kGS];                        // h of each compacted live row
   uint16_t rows[kGB * kGS];                     // compacted live rows: (group in batch) << 6 | neuron
   unsigned long long gmask[kGB];
+  unsigned long long bar;                       // completion of the batch's bulk copies
   int gcnt[kGB], goff[kGB + 1];
   int gsrc[kGB];                                // expert id, -1 = shared expert, -2 = invalid
   int gloc[kGB];                                // the group's index inside its expert
@@ -104,12 +122,56 @@ __device__ __forceinline__ float load_h(const void* h, int64_t idx) {
   return hsd::to_f32<HT>(reinterpret_cast<const HT*>(h)[idx]);
 }
 
+// ---- mbarrier / bulk-copy helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}"
+               ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for the phase with `parity`: false after ~2 s.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > 2000000000ull) return false;
+  return true;
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// One TMA bulk copy global -> this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint32_t bar,
+                                         uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
+}
+
 template <typename HT, typename ST, typename YT, int C>
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>::THREADS)
     sparse_down_decode_kernel(const DecodeParams p) {
-  constexpr int NWC = C / 8;
-  constexpr int NRL = kThreads / NWC;            // row lanes
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  using Cfg = DecodeCfg<C>;
+  constexpr int NWC = Cfg::NWC, NGL = Cfg::NGL, THREADS = Cfg::THREADS, WARPS = Cfg::WARPS;
+  constexpr int HPV = 16 / sizeof(HT);           // h values per 16-byte load
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   DecodeSmem<C>& S = *reinterpret_cast<DecodeSmem<C>*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
 
@@ -122,10 +184,25 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   const int GF = p.F / kGS;
   const int g_lo = static_cast<int>((static_cast<long long>(rank) * p.GT) / kCluster);
   const int g_hi = static_cast<int>((static_cast<long long>(rank + 1) * p.GT) / kCluster);
-
   const int wp = tid % NWC;                       // word of the chunk this thread owns
-  const int rl = tid / NWC;                       // row lane
-  const bool active = wp < nwc;
+  const int gl = tid / NWC;                       // group lane
+  const bool lane_used = gl < NGL;                // (C = 192: threads 504..511 idle)
+  const bool active = lane_used && wp < nwc;
+  constexpr int RB = Cfg::RB;
+  const uint32_t bar = smem_u32(&S.bar);
+  const uint32_t meta_bytes = static_cast<uint32_t>(nwc) * 16;   // 8 outputs x 2 bytes per word
+  const uint32_t row_bytes = static_cast<uint32_t>(nwc) * 4;
+  uint32_t phase = 0;
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // Programmatic dependent launch: let the next kernel in the stream start its launch
+  // now, and wait for the previous one (which produces h / sel / gains) before reading.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const uint64_t pol = evict_first_policy();
 
   float out[8];
 #pragma unroll
@@ -133,45 +210,63 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 
   for (int gb0 = g_lo; gb0 < g_hi; gb0 += kGB) {
     const int ng = min(kGB, g_hi - gb0);
-    // ---- 1. h, live masks and counts, one warp per group
-    for (int gi = warp; gi < ng; gi += kWarps) {
-      const int G = gb0 + gi;
-      int slot, gl, src;
-      if (G < p.topk * GF) {
-        slot = G / GF;
-        gl = G - slot * GF;
-        src = (lane == 0) ? __ldg(p.sel + static_cast<int64_t>(b) * p.topk + slot) : 0;
-        src = __shfl_sync(0xffffffffu, src, 0);
-        if (src < 0 || src >= p.E) {
-          if (lane == 0) hsd_flag_decode(HSD_ERR_INDEX);
-          src = -2;
+    // the previous batch's shared-memory reads come before this batch's bulk copies
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // ---- 1. h columns [64*gb0, 64*(gb0+ng)) of row b, the groups' expert ids and gains
+    {
+      const HT* hrow = reinterpret_cast<const HT*>(p.h) + static_cast<int64_t>(b) * p.NR +
+                       static_cast<int64_t>(gb0) * kGS;
+      for (int v = tid; v < ng * kGS / HPV; v += THREADS) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(hrow) + v);
+        const HT* e = reinterpret_cast<const HT*>(&raw);
+#pragma unroll
+        for (int i = 0; i < HPV; ++i) S.hs[v * HPV + i] = hsd::to_f32<HT>(e[i]);
+      }
+      if (tid < ng) {
+        const int G = gb0 + tid;
+        int slot, loc, src;
+        if (G < p.topk * GF) {
+          slot = G / GF;
+          loc = G - slot * GF;
+          src = __ldg(p.sel + static_cast<int64_t>(b) * p.topk + slot);
+          if (src < 0 || src >= p.E) {
+            hsd_flag_decode(HSD_ERR_INDEX);
+            src = -2;
+          }
+        } else {
+          slot = p.topk;
+          loc = G - p.topk * GF;
+          src = -1;
         }
-      } else {
-        slot = p.topk;
-        gl = G - p.topk * GF;
-        src = -1;
+        S.gsrc[tid] = src;
+        S.gloc[tid] = loc;
+        S.ggain[tid] = __ldg(p.gains + static_cast<int64_t>(b) * (p.topk + 1) + slot);
       }
-      const int64_t hcol = static_cast<int64_t>(b) * p.NR + static_cast<int64_t>(slot) * p.F +
-                           static_cast<int64_t>(gl) * kGS;
-      float v0 = 0.f, v1 = 0.f;
-      if (src != -2) {
-        v0 = load_h<HT>(p.h, hcol + lane);
-        v1 = load_h<HT>(p.h, hcol + 32 + lane);
-      }
-      S.hs[gi * kGS + lane] = v0;
-      S.hs[gi * kGS + 32 + lane] = v1;
+    }
+    __syncthreads();
+    // ---- 2. live masks (one warp per group)
+    for (int gi = warp; gi < ng; gi += WARPS) {
+      const bool valid = S.gsrc[gi] != -2;
+      const float v0 = valid ? S.hs[gi * kGS + lane] : 0.f;
+      const float v1 = valid ? S.hs[gi * kGS + 32 + lane] : 0.f;
       const unsigned long long m = ballot64(v0 != 0.f, v1 != 0.f);
       if (lane == 0) {
         S.gmask[gi] = m;
         S.gcnt[gi] = __popcll(m);
-        S.gsrc[gi] = src;
-        S.gloc[gi] = gl;
-        S.ggain[gi] = __ldg(p.gains + static_cast<int64_t>(b) * (p.topk + 1) + slot);
+      }
+      if (m != 0ull && p.loadsc && lane < 2) {   // a live group's scale (lane 0) / bias (lane 1) chunk
+        const int src = S.gsrc[gi];
+        const int64_t grow = (src >= 0) ? static_cast<int64_t>(src) * GF + S.gloc[gi] : S.gloc[gi];
+        const uint16_t* base = (src >= 0) ? (lane ? p.pb : p.ps) : (lane ? p.spb : p.sps);
+        bulk_g2s((lane ? S.meta_b : S.meta_s) + gi * C, base + grow * p.D + static_cast<int64_t>(w0) * 8,
+                 meta_bytes, bar, pol);
       }
     }
     __syncthreads();
-    // ---- 2. scan the counts (warp 0), then compact the live rows (one warp per group)
-    if (warp == 0) {
+    // ---- 3. the counts' exclusive scan (every warp, redundantly), the compaction and the
+    //         row copies of the first sub-batch
+    int nrows;
+    {
       const int c = (lane < ng) ? S.gcnt[lane] : 0;
       int x = c;
 #pragma unroll
@@ -179,122 +274,131 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
         const int y = __shfl_up_sync(0xffffffffu, x, d);
         if (lane >= d) x += y;
       }
-      if (lane < ng) S.goff[lane] = x - c;
-      if (lane == 31) S.goff[ng] = x;   // (lanes >= ng add zero, so lane 31 holds the total)
-    }
-    __syncthreads();
-    const int nrows = S.goff[ng];
-    for (int gi = warp; gi < ng; gi += kWarps) {
-      const unsigned long long m = S.gmask[gi];
-      const int base = S.goff[gi];
-      if ((m >> lane) & 1ull) S.rows[base + live_prefix(m, lane)] = static_cast<uint16_t>((gi << 6) | lane);
-      if ((m >> (lane + 32)) & 1ull)
-        S.rows[base + live_prefix(m, lane + 32)] = static_cast<uint16_t>((gi << 6) | (lane + 32));
-    }
-    __syncthreads();
-
-    // ---- 3./4. stage and accumulate, sub-batches of kRB rows
-    int gcur = -1;
-    float acc[8], hsum = 0.f;
-#pragma unroll
-    for (int n = 0; n < 8; ++n) acc[n] = 0.f;
-
-    auto flush = [&](int gi) {
-      const float g = S.ggain[gi];
-      if (p.loadsc) {
-        const uint4 s4 = *reinterpret_cast<const uint4*>(&S.meta_s[gi * C + wp * 8]);
-        const uint4 b4 = *reinterpret_cast<const uint4*>(&S.meta_b[gi * C + wp * 8]);
-        const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
-        const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          const float s = hsd::bits16_to_f32<ST>(static_cast<uint16_t>(sw[n >> 1] >> (16 * (n & 1))));
-          const float bb = hsd::bits16_to_f32<ST>(static_cast<uint16_t>(bw[n >> 1] >> (16 * (n & 1))));
-          out[n] = fmaf(g, fmaf(16.f * s, acc[n] - hsum, bb * hsum), out[n]);
-        }
-      } else {
-#pragma unroll
-        for (int n = 0; n < 8; ++n) out[n] = fmaf(g, fmaf(16.f, acc[n] - hsum, hsum), out[n]);
+      const int goff_lane = x - c;
+      nrows = __shfl_sync(0xffffffffu, x, 31);
+      if (warp == 0) {
+        if (lane < ng) S.goff[lane] = goff_lane;
+        if (lane == 0) S.goff[ng] = nrows;
+        // the batch's whole byte count, registered once with the single arrival (copies
+        // already issued may complete first: the phase cannot end before the arrival)
+        const unsigned live_groups = __popc(__ballot_sync(0xffffffffu, c > 0));
+        if (lane == 0 && nrows > 0)
+          mbar_arrive_expect_tx(bar, (p.loadsc ? live_groups * 2u * meta_bytes : 0u) +
+                                         static_cast<uint32_t>(min(nrows, RB)) * row_bytes);
       }
-    };
-
-    for (int r0 = 0; r0 < nrows; r0 += kRB) {
-      const int rn = min(kRB, nrows - r0);
-      if (r0 == 0 && p.loadsc) {                 // the batch's live groups' scale / bias chunks
-        // one 16-byte piece = the 8 scales (or biases) of one word's 8 outputs
-        for (int t = tid; t < ng * 2 * nwc; t += kThreads) {
-          const int gi = t / (2 * nwc);
-          const int rem = t - gi * 2 * nwc;
-          const int which = rem / nwc, pc = rem - which * nwc;
-          if (S.gcnt[gi] == 0) continue;
-          const int src = S.gsrc[gi];
-          const int64_t grow = (src >= 0) ? static_cast<int64_t>(src) * GF + S.gloc[gi] : S.gloc[gi];
-          const uint16_t* base = (src >= 0) ? (which ? p.pb : p.ps) : (which ? p.spb : p.sps);
-          const uint16_t* g = base + grow * p.D + static_cast<int64_t>(w0 + pc) * 8;
-          uint16_t* d = (which ? S.meta_b : S.meta_s) + gi * C + pc * 8;
-          hsd::cp_async16(d, g);
+      for (int gi = warp; gi < ng; gi += WARPS) {
+        const unsigned long long m = S.gmask[gi];
+        const int base = __shfl_sync(0xffffffffu, goff_lane, gi);
+        const int src = S.gsrc[gi];
+        const int64_t rowbase = (src >= 0) ? (static_cast<int64_t>(src) * p.F + static_cast<int64_t>(S.gloc[gi]) * kGS)
+                                           : static_cast<int64_t>(S.gloc[gi]) * kGS;
+        const uint32_t* wbase = (src >= 0) ? p.pw : p.spw;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int j = lane + 32 * half;
+          if ((m >> j) & 1ull) {
+            const int idx = base + live_prefix(m, j);
+            S.rows[idx] = static_cast<uint16_t>((gi << 6) | j);
+            S.hrow[idx] = S.hs[gi * kGS + j];
+            if (idx < RB) bulk_g2s(&S.stage[idx * NWC], wbase + (rowbase + j) * p.NW + w0, row_bytes, bar, pol);
+          }
         }
       }
-      {                                          // the sub-batch's live row chunks
-        const int pieces = nwc / 4;              // 16-byte pieces per row chunk
-        for (int t = tid; t < rn * pieces; t += kThreads) {
-          const int r = t / pieces, pc = t - r * pieces;
+    }
+    __syncthreads();
+
+    // ---- 4. per sub-batch of RB rows: wait for the copies, accumulate from shared memory
+    for (int r0 = 0; r0 < nrows; r0 += RB) {
+      const int rn = min(RB, nrows - r0);
+      if (r0 > 0) {                              // later sub-batches (dense h only)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (tid == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(rn) * row_bytes);
+        for (int r = tid; r < rn; r += THREADS) {
           const int code = S.rows[r0 + r];
           const int gi = code >> 6, j = code & 63;
           const int src = S.gsrc[gi];
           const int64_t neuron = static_cast<int64_t>(S.gloc[gi]) * kGS + j;
           const uint32_t* g = (src >= 0) ? p.pw + (static_cast<int64_t>(src) * p.F + neuron) * p.NW
                                          : p.spw + neuron * p.NW;
-          hsd::cp_async16(&S.stage[r * NWC + pc * 4], g + w0 + pc * 4);
+          bulk_g2s(&S.stage[r * NWC], g + w0, row_bytes, bar, pol);
         }
       }
-      hsd::cp_async_commit();
-      hsd::cp_async_wait_all();
-      __syncthreads();
+      if (!mbar_wait_bounded(bar, phase)) {
+        if (tid == 0) hsd_flag_decode(HSD_ERR_TIMEOUT);
+        mbar_wait_bounded(bar, phase);           // once more for the copies still in flight
+      }
+      phase ^= 1u;
       if (active) {
-        for (int r = rl; r < rn; r += NRL) {
-          const int code = S.rows[r0 + r];
-          const int gi = code >> 6;
-          const float hv = S.hs[gi * kGS + (code & 63)];
-          const uint32_t q = S.stage[r * NWC + wp];
-          if (gi != gcur) {
-            if (gcur >= 0) flush(gcur);
-            gcur = gi;
-            hsum = 0.f;
+        for (int gi = gl; gi < ng; gi += NGL) {
+          const int j0 = max(S.goff[gi], r0), j1 = min(S.goff[gi + 1], r0 + rn);
+          if (j0 >= j1) continue;
+          float acc[8], hsum = 0.f;
 #pragma unroll
-            for (int n = 0; n < 8; ++n) acc[n] = 0.f;
+          for (int n = 0; n < 8; ++n) acc[n] = 0.f;
+          for (int r = j0; r < j1; ++r) {
+            const float hv = S.hrow[r];
+            const uint32_t q = S.stage[(r - r0) * NWC + wp];
+            hsum += hv;
+            acc[0] = fmaf(hv, nib_unit<0>(q), acc[0]);
+            acc[1] = fmaf(hv, nib_unit<1>(q), acc[1]);
+            acc[2] = fmaf(hv, nib_unit<2>(q), acc[2]);
+            acc[3] = fmaf(hv, nib_unit<3>(q), acc[3]);
+            acc[4] = fmaf(hv, nib_unit<4>(q), acc[4]);
+            acc[5] = fmaf(hv, nib_unit<5>(q), acc[5]);
+            acc[6] = fmaf(hv, nib_unit<6>(q), acc[6]);
+            acc[7] = fmaf(hv, nib_unit<7>(q), acc[7]);
           }
-          hsum += hv;
-          acc[0] = fmaf(hv, nib_unit<0>(q), acc[0]);
-          acc[1] = fmaf(hv, nib_unit<1>(q), acc[1]);
-          acc[2] = fmaf(hv, nib_unit<2>(q), acc[2]);
-          acc[3] = fmaf(hv, nib_unit<3>(q), acc[3]);
-          acc[4] = fmaf(hv, nib_unit<4>(q), acc[4]);
-          acc[5] = fmaf(hv, nib_unit<5>(q), acc[5]);
-          acc[6] = fmaf(hv, nib_unit<6>(q), acc[6]);
-          acc[7] = fmaf(hv, nib_unit<7>(q), acc[7]);
+          // the affine form is linear in the row set, so a group split across
+          // sub-batches is folded in piece by piece
+          const float g = S.ggain[gi];
+          if (p.loadsc) {
+            const uint4 s4 = *reinterpret_cast<const uint4*>(&S.meta_s[gi * C + wp * 8]);
+            const uint4 b4 = *reinterpret_cast<const uint4*>(&S.meta_b[gi * C + wp * 8]);
+            const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
+            const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+              const float sc = hsd::bits16_to_f32<ST>(static_cast<uint16_t>(sw[n >> 1] >> (16 * (n & 1))));
+              const float bi = hsd::bits16_to_f32<ST>(static_cast<uint16_t>(bw[n >> 1] >> (16 * (n & 1))));
+              out[n] = fmaf(g, fmaf(16.f * sc, acc[n] - hsum, bi * hsum), out[n]);
+            }
+          } else {
+#pragma unroll
+            for (int n = 0; n < 8; ++n) out[n] = fmaf(g, fmaf(16.f, acc[n] - hsum, hsum), out[n]);
+          }
         }
       }
-      __syncthreads();                           // stage is rewritten by the next sub-batch
+      __syncthreads();                           // stage / meta / hs are rewritten next
     }
-    if (active && gcur >= 0) flush(gcur);
-    __syncthreads();                             // meta / hs / rows are rewritten by the next batch
   }
 
-  // ---- 5. reduce the row lanes (fixed order) into S.part, reusing the stage buffer
-  float* red = reinterpret_cast<float*>(S.stage);   // [NRL][C] fp32 (NRL*C = 2*kThreads*... fits)
-#pragma unroll
-  for (int n = 0; n < 8; ++n) red[rl * C + wp * 8 + n] = out[n];
+  // ---- 5. reduce the group lanes (fixed order) into S.part, reusing the stage buffer
+  float* red = reinterpret_cast<float*>(S.stage);   // [NGL][C] fp32
+  static_assert(sizeof(float) * Cfg::NGL * C <= sizeof(uint32_t) * Cfg::RB * Cfg::NWC,
+                "group-lane reduction must fit in the stage buffer");
+  if (lane_used) {
+    *reinterpret_cast<float4*>(&red[gl * C + wp * 8]) = make_float4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<float4*>(&red[gl * C + wp * 8 + 4]) = make_float4(out[4], out[5], out[6], out[7]);
+  }
   __syncthreads();
-  for (int o = tid; o < C; o += kThreads) {
-    float t = 0.f;
-    for (int l = 0; l < NRL; ++l) t += red[l * C + o];
-    S.part[o] = t;
+  {                                              // 4 partial sums per output, then their sum
+    constexpr int NP = 4, PER = (NGL + NP - 1) / NP;
+    float* red2 = S.hs;                          // [NP][C] (hs is free now)
+    for (int t = tid; t < NP * C; t += THREADS) {
+      const int o = t % C, q = t / C;
+      float a = 0.f;
+#pragma unroll
+      for (int l = q * PER; l < min(NGL, (q + 1) * PER); ++l) a += red[l * C + o];
+      red2[q * C + o] = a;
+    }
+    __syncthreads();
+    for (int o = tid; o < C; o += THREADS)
+      S.part[o] = (red2[o] + red2[C + o]) + (red2[2 * C + o] + red2[3 * C + o]);
   }
   // ---- 6. the cluster's 8 partials, summed in rank order through DSMEM
   cluster.sync();
   constexpr int per = C / kCluster;
-  for (int i = tid; i < per; i += kThreads) {
+  for (int i = tid; i < per; i += THREADS) {
     const int o = rank * per + i;
     if (o < nwc * 8) {
       float t = 0.f;
@@ -309,15 +413,18 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
 }
 
 // ---- active-index sets, the same ballot compaction per (token, slot)
+constexpr int kLiveThreads = 256;
+constexpr int kWarps = kLiveThreads / 32;
+
 template <typename HT>
-__global__ void __launch_bounds__(kThreads) live_rows_kernel(const void* h, int32_t* live,
+__global__ void __launch_bounds__(kLiveThreads) live_rows_kernel(const void* h, int32_t* live,
                                                              int32_t* count, int F, int FS, int topk) {
   const int slot = blockIdx.x, b = blockIdx.y;
   const int width = (slot < topk) ? F : FS;
   const int NR = topk * F + FS;
   const int maxw = max(F, FS);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  __shared__ int wcnt[kThreads / 32];
+  __shared__ int wcnt[kWarps];
   __shared__ int base_s;
   if (threadIdx.x == 0) base_s = 0;
   __syncthreads();
@@ -350,10 +457,9 @@ __global__ void __launch_bounds__(kThreads) live_rows_kernel(const void* h, int3
 
 template <typename HT, typename ST, typename YT, int C>
 int launch_decode(const DecodeParams& p, cudaStream_t st) {
+  using Cfg = DecodeCfg<C>;
   auto kern = sparse_down_decode_kernel<HT, ST, YT, C>;
   const size_t smem = sizeof(DecodeSmem<C>);
-  static_assert(sizeof(float) * (kThreads / (C / 8)) * C <= sizeof(uint32_t) * kRB * (C / 8),
-                "row-lane reduction must fit in the stage buffer");
   static int configured_device = -1;           // the attribute is set once per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -363,18 +469,43 @@ int launch_decode(const DecodeParams& p, cudaStream_t st) {
     if (e != cudaSuccess) return hsd::check_cuda(e, "hsd_sparse_down_decode: smem attribute");
     configured_device = dev;
   }
-  const int nch = (p.NW + (C / 8) - 1) / (C / 8);
-  dim3 grid(nch * kCluster, p.B);
-  kern<<<grid, kThreads, smem, st>>>(p);
-  return hsd::check_launch("hsd_sparse_down_decode");
+  const int nch = (p.NW + Cfg::NWC - 1) / Cfg::NWC;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nch * kCluster, p.B);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // overlap with the previous launch
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return hsd::check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "hsd_sparse_down_decode launch");
+}
+
+// Output chunk width (outputs per cluster): 192 (112 CTAs per token, one per SM) for
+// B <= 2, where a token's CTAs should not share SMs; 128 (168 CTAs per token) above.
+// HSD_DECODE_CHUNK=128 or 192 forces one for tuning.
+inline int chunk_choice(int B) {
+  static int forced = [] {
+    const char* e = getenv("HSD_DECODE_CHUNK");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 128 || forced == 192) return forced;
+  return B <= 2 ? 192 : 128;
+}
+
+template <typename HT, typename ST, typename YT>
+int dispatch_c(const DecodeParams& p, cudaStream_t st) {
+  return chunk_choice(p.B) == 192 ? launch_decode<HT, ST, YT, 192>(p, st) : launch_decode<HT, ST, YT, 128>(p, st);
 }
 
 template <typename HT, typename ST>
 int dispatch_y(int y_dtype, const DecodeParams& p, cudaStream_t st) {
   switch (y_dtype) {
-    case HSD_F32: return launch_decode<HT, ST, float, 128>(p, st);
-    case HSD_F16: return launch_decode<HT, ST, __half, 128>(p, st);
-    case HSD_BF16: return launch_decode<HT, ST, __nv_bfloat16, 128>(p, st);
+    case HSD_F32: return dispatch_c<HT, ST, float>(p, st);
+    case HSD_F16: return dispatch_c<HT, ST, __half>(p, st);
+    case HSD_BF16: return dispatch_c<HT, ST, __nv_bfloat16>(p, st);
   }
   return hsd::set_error(HSD_ERR_DTYPE, "hsd_sparse_down_decode: y_dtype %d", y_dtype);
 }
@@ -407,10 +538,10 @@ extern "C" int hsd_sparse_down_decode(const void* h, int h_dtype, const int32_t*
   const long long NR = static_cast<long long>(topk) * F + FS;
   if (NR > (1ll << 30) || static_cast<long long>(E) * F * (D / 8) > (1ll << 40))
     return hsd::set_error(HSD_ERR_SHAPE, "hsd_sparse_down_decode: sizes too large");
-  const void* ptr16[] = {pw, ps, pb, spw, sps, spb};
+  const void* ptr16[] = {h, pw, ps, pb, spw, sps, spb};
   for (const void* q : ptr16)
     if (!hsd::aligned(q, 16))
-      return hsd::set_error(HSD_ERR_ALIGN, "hsd_sparse_down_decode: weight pointers must be 16-byte aligned");
+      return hsd::set_error(HSD_ERR_ALIGN, "hsd_sparse_down_decode: h and the weight pointers must be 16-byte aligned");
   DecodeParams p;
   p.h = h; p.sel = sel; p.gains = gains; p.pw = pw;
   p.ps = static_cast<const uint16_t*>(ps); p.pb = static_cast<const uint16_t*>(pb);
@@ -437,10 +568,10 @@ extern "C" int hsd_decode_live_rows(const void* h, int h_dtype, int32_t* live, i
   dim3 grid(topk + 1, B);
   cudaStream_t st = hsd::as_stream(stream);
   switch (h_dtype) {
-    case HSD_F32: live_rows_kernel<float><<<grid, kThreads, 0, st>>>(h, live, count, F, FS, topk); break;
-    case HSD_F16: live_rows_kernel<__half><<<grid, kThreads, 0, st>>>(h, live, count, F, FS, topk); break;
+    case HSD_F32: live_rows_kernel<float><<<grid, kLiveThreads, 0, st>>>(h, live, count, F, FS, topk); break;
+    case HSD_F16: live_rows_kernel<__half><<<grid, kLiveThreads, 0, st>>>(h, live, count, F, FS, topk); break;
     case HSD_BF16:
-      live_rows_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(h, live, count, F, FS, topk);
+      live_rows_kernel<__nv_bfloat16><<<grid, kLiveThreads, 0, st>>>(h, live, count, F, FS, topk);
       break;
     default: return hsd::set_error(HSD_ERR_DTYPE, "hsd_decode_live_rows: h_dtype %d", h_dtype);
   }
