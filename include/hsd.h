@@ -105,6 +105,46 @@ int hsd_sparse_down_decode(const void* h, int h_dtype, const int32_t* sel,
 int hsd_decode_live_rows(const void* h, int h_dtype, int32_t* live, int32_t* count, int B,
                          int F, int FS, int topk, void* stream);
 
+/* ---- prefill: hsd/prefill.py --------------------------------------------------- */
+
+/* The fixed tile count of build_tiles (hsd/prefill.py:266,275): nt_routed =
+ * T*topk/tt + E (+1 when E < tt), nt_shared = ceil(T/tt). Host-only, no device work. */
+int hsd_prefill_num_tiles(int T, int topk, int E, int tt, int* nt_routed, int* nt_shared);
+
+/* hsd/prefill.py:247 build_tiles(sel, E, tt):
+ *   sel [T, topk] int32 -> tile_e [NT] int32 (expert, E = shared, -1 = empty),
+ *   tile_slot [NT*tt] int32 (slot t*topk+k for routed tiles, token t for shared tiles,
+ *   -1 padding), NT = nt_routed + nt_shared. Inside an expert, slots keep ascending order.
+ *   E <= 256. An expert id outside [0, E) is recorded in the status word and its slot dropped. */
+int hsd_prefill_build_tiles(const int32_t* sel, int T, int topk, int E, int tt, int32_t* tile_e,
+                            int32_t* tile_slot, void* stream);
+
+/* hsd/prefill.py:281 build_union(h, tile_e, tile_slot, *, F, FS, topk, E, tt, kc, nth):
+ *   ulist [NT, umax] int32: per tile the ascending union of the columns nonzero in any of
+ *   its slots (-1 padded), ucount [NT] int32. umax >= max(F, FS); tt <= 1024. */
+int hsd_prefill_build_union(const void* h, int h_dtype, const int32_t* tile_e,
+                            const int32_t* tile_slot, int NT, int tt, int F, int FS, int topk,
+                            int E, int umax, int32_t* ulist, int32_t* ucount, void* stream);
+
+/* Workspace bytes hsd_sparse_down_prefill needs for (T, D, F, FS, topk, E): the gathered
+ * fp16 A rows of every tile and the fp32 partial rows [T*(topk+1), D]. Host-only. */
+int hsd_prefill_workspace_bytes(int T, int D, int F, int FS, int topk, int E, size_t* bytes);
+
+/* hsd/prefill.py:294 sparse_down_prefill(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS,
+ * D, topk, E, tt, nb, kc, nsg, tiles, union, out_dtype):
+ *   h [T, topk*F+FS], gains [T, topk+1] f32, tiles from hsd_prefill_build_tiles with
+ *   tt = 128, layouts as for decode -> y [T, D] (+ resid). Gathers the tiles' h rows (fp16),
+ *   runs the tcgen05 grouped GEMM (weights dequantised to fp16 in shared memory, fp32
+ *   accumulation in TMEM, routing gain in the epilogue) and sums each token's topk+1
+ *   partial rows in a fixed order. The caller provides `workspace` (16-byte aligned) of at
+ *   least hsd_prefill_workspace_bytes(). Supported: D % 192 == 0, F % 64 == 0, FS % 64 == 0. */
+int hsd_sparse_down_prefill(const void* h, int h_dtype, const float* gains, const int32_t* tile_e,
+                            const int32_t* tile_slot, int NT, const uint32_t* pw, const void* ps,
+                            const void* pb, int s_dtype, const uint32_t* spw, const void* sps,
+                            const void* spb, const void* resid, void* y, int y_dtype, int T, int D,
+                            int F, int FS, int topk, int E, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

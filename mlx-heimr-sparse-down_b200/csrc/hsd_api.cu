@@ -22,6 +22,7 @@ int set_error(int code, const char* fmt, ...) {
 // status readers defined by HSD_DEFINE_STATUS in the kernel translation units
 int hsd_read_status_decode(int* out, cudaStream_t st);
 int hsd_read_status_prefill(int* out, cudaStream_t st);
+int hsd_read_status_gemm(int* out, cudaStream_t st);
 
 extern "C" const char* hsd_last_error_string(void) { return hsd::g_last_error; }
 
@@ -31,7 +32,8 @@ extern "C" int hsd_device_status(int* status_out, void* stream) {
   if (!status_out) return hsd::set_error(HSD_ERR_ARG, "hsd_device_status: null output");
   cudaStream_t st = hsd::as_stream(stream);
   int first = HSD_OK;
-  int (*readers[])(int*, cudaStream_t) = {hsd_read_status_decode, hsd_read_status_prefill};
+  int (*readers[])(int*, cudaStream_t) = {hsd_read_status_decode, hsd_read_status_prefill,
+                                                hsd_read_status_gemm};
   for (auto rd : readers) {
     int v = HSD_OK;
     int rc = rd(&v, st);

@@ -1,0 +1,29 @@
+// Declarations shared by the prefill translation units.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hsd {
+
+// Tiles of the fixed tile order for (T, topk, E, tt): routed, then shared.
+int prefill_tile_counts(int T, int topk, int E, int tt, int* nt_routed, int* nt_shared);
+
+// hc[tile*tt + m, c] = fp16(h[slot's columns][c]) for the rows of non-empty tiles.
+int launch_gather(const void* h, int h_dtype, const int32_t* tile_e, const int32_t* tile_slot, int NT,
+                  int tt, int F, int FS, int topk, int E, int kmax, __half* hc, cudaStream_t st);
+
+// y[t] = sum over the token's topk + 1 partial rows (+ resid), fixed order.
+int launch_reduce(const float* part, const void* resid, void* y, int y_dtype, int T, int D, int topk,
+                  cudaStream_t st);
+
+// The tensor-core grouped GEMM over the tile order (hsd_prefill_gemm.cu).
+int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const int32_t* tile_slot, int NT,
+                        const float* gains, const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
+                        const uint32_t* spw, const void* sps, const void* spb, float* part, int T, int D,
+                        int F, int FS, int topk, int E, cudaStream_t st);
+
+constexpr int kPrefillTile = 128;   // slots per tile of the GEMM (its M)
+
+}  // namespace hsd

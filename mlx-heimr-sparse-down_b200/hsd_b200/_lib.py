@@ -33,6 +33,12 @@ SIGNATURES = {
     "hsd_sparse_down_decode": [_P, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I,
                                _I, _I, _I, _I, _I, _I, _I, _P],
     "hsd_decode_live_rows": [_P, _I, _P, _P, _I, _I, _I, _I, _P],
+    "hsd_prefill_num_tiles": [_I, _I, _I, _I, _P, _P],
+    "hsd_prefill_build_tiles": [_P, _I, _I, _I, _I, _P, _P, _P],
+    "hsd_prefill_build_union": [_P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P],
+    "hsd_prefill_workspace_bytes": [_I, _I, _I, _I, _I, _I, _P],
+    "hsd_sparse_down_prefill": [_P, _I, _P, _P, _P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I,
+                                _I, _I, _I, _I, _I, _I, _P, ctypes.c_size_t, _P],
 }
 
 _lib = None

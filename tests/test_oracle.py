@@ -127,3 +127,40 @@ def test_live_rows_and_byte_model():
     # rows: (0,1),(0,5),(0,64) for token 0 slot 0; (0,1) again for token 1 -> union 3; shared 2
     assert nb["rows"] == 3 + 2
     assert nb["groups"] == 2 + 2   # (0,0),(0,1) routed; (-1,0),(-1,1) shared
+
+
+def test_prefill_tiles_oracle_properties():
+    """The tile order restatement: every routed slot appears exactly once, in a tile of its
+    expert, ascending inside the expert; shared tiles hold every token once."""
+    from oracle import prefill as op
+    rng = np.random.default_rng(2)
+    T, K, E, tt = 100, 6, 16, 32
+    sel = np.stack([rng.permutation(E)[:K] for _ in range(T)]).astype(np.int32)
+    te, ts = op.build_tiles(sel, E, tt)
+    nr, ns = op.num_tiles(T, K, E, tt)
+    assert te.shape == (nr + ns,) and ts.shape == ((nr + ns) * tt,)
+    routed = ts[:nr * tt]
+    seen = routed[routed >= 0]
+    assert sorted(seen.tolist()) == list(range(T * K))
+    for t in range(nr):
+        sl = ts[t * tt:(t + 1) * tt]
+        sl = sl[sl >= 0]
+        if te[t] < 0:
+            assert sl.size == 0
+        else:
+            assert np.all(sel.reshape(-1)[sl] == te[t]) and np.all(np.diff(sl) > 0)
+    assert np.all(te[nr:] == E)
+    sh = ts[nr * tt:]
+    assert sorted(sh[sh >= 0].tolist()) == list(range(T))
+
+
+def test_prefill_union_oracle_small():
+    from oracle import prefill as op
+    h = np.zeros((2, 2 * 64 + 64), np.float32)
+    h[0, 3] = 1; h[1, 64 + 7] = 1; h[1, 128 + 5] = 1
+    sel = np.array([[0, 1], [1, 0]], np.int32)
+    te, ts = op.build_tiles(sel, 2, 4)
+    ul, uc = op.build_union(h, te, ts, F=64, FS=64, topk=2, E=2, tt=4, umax=64)
+    # expert 0: slots 0 (t0,k0: col 3) and 3 (t1,k1: col 7) -> [3, 7]; expert 1: slots 1, 2 -> []
+    assert list(ul[0, :uc[0]]) == [3, 7] and uc[1] == 0 and np.all(ul[1] == -1)
+    assert list(ul[te.tolist().index(2), :1]) == [5]
