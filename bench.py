@@ -290,6 +290,48 @@ def cpu_leg(layers, wl, budget_s=10.0, n_layers=4):
     return nbytes / dt / 1e9, cores, sample
 
 
+def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512):
+    """Config 2: T tokens in chunks of `chunk` through one MoE layer (layer 0), Zipf(1.1)
+    routing, h = relu(N(-1.28, 1))^2. Times tile order + gather + tcgen05 GEMM + reduce per
+    chunk (CUDA events, max over ranks) -> dict with tensor-pipe and byte rates."""
+    from hsd_b200 import prefill as hp
+    gen = torch.Generator(device=device).manual_seed(77)
+    sel, sc = synth.route_zipf(T, E, TOPK, gen, device)
+    gains = torch.cat([sc, torch.ones((T, 1), device=device)], 1).contiguous()
+    h = synth.relu2_activations((T, TOPK * F + FS), 0.90, gen, device)
+    lay = layers[0]
+    y = torch.empty((T, D), dtype=torch.bfloat16, device=device)
+    ws = torch.empty(hp.workspace_bytes(chunk, D, F, FS, TOPK, E), dtype=torch.uint8, device=device)
+    chunks = [(i, min(T, i + chunk)) for i in range(0, T, chunk)]
+
+    def run(_):
+        for a, b in chunks:
+            hp.sparse_down_prefill(h[a:b], sel[a:b], gains[a:b], *lay, F=F, FS=FS, D=D, topk=TOPK, E=E,
+                                   out=y[a:b], workspace=ws)
+
+    ms = timed(run, reps, 3, device, dist_on) / reps
+    # executed MMA work: every non-empty tile is 128 slots x its K x D
+    ex = 0
+    for a, b in chunks:
+        te, _ = hp.build_tiles(sel[a:b].contiguous(), E, hp.GEMM_TT)
+        te = te.cpu()
+        n_routed = int(((te >= 0) & (te < E)).sum())
+        n_shared = int((te == E).sum())
+        ex += 2.0 * hp.GEMM_TT * D * (n_routed * F + n_shared * FS)
+    dense = 2.0 * T * (TOPK * F + FS) * D
+    peak_t = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["bf16_tflops"] \
+        if os.path.exists(os.path.join(REPO, "MEASURED_PEAKS.json")) else 1590.0
+    wbytes = len(chunks) * (E * F * D // 2 + E * (F // 64) * D * 4 + FS * D // 2 + (FS // 64) * D * 4)
+    return {"workload": f"config2: {T} tokens in chunks of {chunk}, one MoE layer, Zipf(1.1) top-6, z=0.90",
+            "ms": ms, "tokens_per_s": T / (ms / 1e3),
+            "dense_equiv_tflops": dense / (ms / 1e3) / 1e12,
+            "executed_mma_tflops": ex / (ms / 1e3) / 1e12,
+            "tensor_frac_of_measured_bf16": ex / (ms / 1e3) / 1e12 / peak_t,
+            "weight_GBps": wbytes / (ms / 1e3) / 1e9,
+            "note": "executed = 128-slot tiles incl. padding (fp16 operands, fp32 accumulate); "
+                    "dense_equiv = 2*T*(6F+FS)*D"}
+
+
 def traffic_from_profile():
     """Per-launch DRAM traffic of the decode kernel from the committed ncu summary."""
     p = os.path.join(REPO, "profiles", "decode_sparse_down_ncu.md")
@@ -312,6 +354,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--layers", type=int, default=23, help="fewer layers: small profiling case only")
     args = ap.parse_args()
@@ -390,6 +433,10 @@ def main():
                               "GBps": w2.bytes_per_step * k / (m2 / 1e3) / 1e9})
                 del w2
 
+    prefill = None
+    if not args.no_prefill:
+        prefill = prefill_leg(layers, device, dist_on)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         v, cores, sample = cpu_leg(layers, wl, budget_s=args.cpu_seconds)
@@ -415,6 +462,7 @@ def main():
         "clocks": clk.summary(),
         "us_per_layer": launch_ms * 1e3,
         "sweep": sweep,
+        "prefill": prefill,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
