@@ -145,6 +145,29 @@ int hsd_sparse_down_prefill(const void* h, int h_dtype, const float* gains, cons
                             int F, int FS, int topk, int E, void* workspace, size_t workspace_bytes,
                             void* stream);
 
+/* ---- allocation-free prefill ------------------------------------------------------ */
+
+/* No counterpart in the reference. For callers that cannot call cudaMalloc (code running
+ * under CUDA graph capture without a memory pool, runtimes that own all device memory,
+ * hosts that must not grow device memory after start-up): the same computation as
+ * hsd_sparse_down_prefill, with its scratch in one fixed device array inside this library
+ * (hsd_prefill_noalloc_max_bytes() bytes, 64 MiB, held by every GPU that loads the library
+ * until exit) instead of a caller workspace. The caller still passes inputs and outputs,
+ * tiles built with tt = 128. A call whose scratch would exceed the array returns
+ * HSD_ERR_SHAPE with the bytes it needs (at the reference shapes: up to about 11 tokens;
+ * a model with fewer experts or narrower layers admits more). The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture. Calls share the array: calls whose work
+ * overlaps on the GPU (different streams or host threads) race; calls ordered on one
+ * stream do not. Allocates nothing, frees nothing. */
+int hsd_prefill_noalloc_max_bytes(size_t* bytes);
+int hsd_sparse_down_prefill_noalloc(const void* h, int h_dtype, const float* gains,
+                                    const int32_t* tile_e, const int32_t* tile_slot, int NT,
+                                    const uint32_t* pw, const void* ps, const void* pb,
+                                    int s_dtype, const uint32_t* spw, const void* sps,
+                                    const void* spb, const void* resid, void* y, int y_dtype,
+                                    int T, int D, int F, int FS, int topk, int E, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
