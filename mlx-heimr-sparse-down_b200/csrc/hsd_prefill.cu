@@ -189,7 +189,7 @@ __global__ void __launch_bounds__(256) gather_kernel(const HT* __restrict__ h,
 
 // y[t, o] = sum_{p = 0..topk} part[t*(topk+1) + p, o] (+ resid), fixed order.
 template <typename YT>
-__global__ void __launch_bounds__(256) reduce_kernel(const float* __restrict__ part, const void* resid,
+__global__ void __launch_bounds__(256) partial_reduce_kernel(const float* __restrict__ part, const void* resid,
                                                      void* y, int T, int D, int topk) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
   if (i >= static_cast<int64_t>(T) * D) return;
@@ -246,9 +246,9 @@ int launch_reduce(const float* part, const void* resid, void* y, int y_dtype, in
   const int64_t n = static_cast<int64_t>(T) * D;
   const unsigned grid = static_cast<unsigned>((n + 255) / 256);
   switch (y_dtype) {
-    case HSD_F32: reduce_kernel<float><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk); break;
-    case HSD_F16: reduce_kernel<__half><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk); break;
-    case HSD_BF16: reduce_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk); break;
+    case HSD_F32: partial_reduce_kernel<float><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk); break;
+    case HSD_F16: partial_reduce_kernel<__half><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk); break;
+    case HSD_BF16: partial_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk); break;
     default: return set_error(HSD_ERR_DTYPE, "prefill reduce: y_dtype %d", y_dtype);
   }
   return check_launch("prefill reduce");

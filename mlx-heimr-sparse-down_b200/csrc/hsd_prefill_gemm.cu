@@ -6,7 +6,7 @@
 //   A [128 slots x 64] fp16   the gathered h rows (hc), TMA 2D load, 128-byte swizzle (K-major)
 //   W [64 neurons x 24 words] the packed 4-bit rows of the block, TMA 2D load (no swizzle)
 //   s, b [192]                the group's scales / biases of the block, two bulk copies
-//   B [64 x 192] fp16         dequantised in shared memory by 8 warps, s*q + b with one
+//   B [64 x 192] fp16         dequantised in shared memory by 12 warps, s*q + b with one
 //                             fp16 rounding (half2 FMA), written MN-major with the 128-byte
 //                             swizzle the tensor core reads
 //   D [128 x 192] fp32 += A . B, tcgen05.mma.cta_group::1.kind::f16 issued by one thread,
@@ -16,8 +16,9 @@
 // slot's routing gain, stored to part[token*(topk+1) + k, :] (fp32). A separate fixed-order
 // reduce sums the topk+1 partial rows of each token.
 //
-// Warp roles (14 warps): 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-5 epilogue, 6-13
-// dequantisation. Stages ring through 4 buffers with full / empty mbarriers. Every mbarrier
+// Warp roles (19 warps): 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-5 epilogue, 6 scale
+// converter (bf16 -> fp16 pairs), 7-18 dequantisation. A / packed-W stages ring through 7 buffers, dequantised B through 2, each
+// with full / empty mbarriers. Every mbarrier
 // wait is bounded (2 s of %globaltimer); running out sets HSD_ERR_TIMEOUT in the status word
 // and the role stops; TMEM is freed after a bounded wait for the epilogue. No multicast.
 #include <cuda.h>
@@ -30,27 +31,38 @@ HSD_DEFINE_STATUS(gemm)
 
 namespace {
 
-constexpr int BM = 128, BN = 192, BK = 64, STAGES = 4;
-constexpr int NWARPS = 14, THREADS = NWARPS * 32;
-constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_EPI0 = 2, WARP_DQ0 = 6, DQ_WARPS = 8;
+constexpr int BM = 128, BN = 192, BK = 64;
+constexpr int STAGES = 7;                                     // A / packed-W / scale stages in flight
+constexpr int BSTAGES = 2;                                    // dequantised B buffers
+constexpr int DQ_WARPS = 12;
+constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_EPI0 = 2, WARP_CONV = 6, WARP_DQ0 = 7;
+constexpr int NWARPS = WARP_DQ0 + DQ_WARPS, THREADS = NWARPS * 32;
+constexpr int DQ_THREADS = DQ_WARPS * 32;
 constexpr int WPB = BN / 8;                                   // packed words per row of a block (24)
 constexpr uint32_t A_BYTES = BM * BK * 2;                     // 16 KB
 constexpr uint32_t B_BYTES = BK * BN * 2;                     // 24 KB
 constexpr uint32_t W_BYTES = BK * WPB * 4;                    // 6 KB
-constexpr uint32_t SB_BYTES = 2 * BN * 2;                     // 768 B
+constexpr uint32_t SB_BYTES = 2 * BN * 2;                     // 768 B (scales then biases)
 constexpr uint32_t TX_BYTES = A_BYTES + W_BYTES + SB_BYTES;
 constexpr uint32_t OFF_A = 0;
 constexpr uint32_t OFF_B = OFF_A + STAGES * A_BYTES;
-constexpr uint32_t OFF_W = OFF_B + STAGES * B_BYTES;
+constexpr uint32_t OFF_W = OFF_B + BSTAGES * B_BYTES;
 constexpr uint32_t OFF_SB = OFF_W + STAGES * W_BYTES;
-constexpr uint32_t OFF_BAR = OFF_SB + STAGES * SB_BYTES;       // 8-byte barriers
-constexpr int NBARS = 3 * STAGES + 2 + 2 + 1;                 // full_tma, full_b, empty, acc_full, acc_empty, done
+constexpr uint32_t OFF_SBH = OFF_SB + STAGES * SB_BYTES;      // fp16 scale / bias pairs per stage
+constexpr uint32_t OFF_BAR = OFF_SBH + STAGES * SB_BYTES;     // 8-byte barriers
+// full_tma[STAGES], empty[STAGES], bfull[BSTAGES], bempty[BSTAGES], acc_full[2], acc_empty[2], done,
+// conv[STAGES]
+constexpr int NBARS = 2 * STAGES + 2 * BSTAGES + 2 + 2 + 1 + STAGES;
 constexpr uint32_t OFF_TMEM = OFF_BAR + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_TMEM + 16 + 1024;         // + slack for 1024-byte alignment
 constexpr uint32_t TMEM_COLS = 512, ACC_COLS = 256;
 constexpr uint32_t B_LBO = (BK / 8) * 1024;                   // B: bytes between 64-column atoms
 static_assert(B_BYTES == (BN / 64) * B_LBO, "B tile = N atoms x K groups");
 static_assert(BN % 64 == 0 && BN <= 256 && BN % 16 == 0, "UMMA N");
+static_assert(OFF_B % 1024 == 0 && A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzled tiles 1024-aligned");
+static_assert((BK * WPB) % DQ_THREADS == 0 && DQ_THREADS % WPB == 0,
+              "dequant: a whole number of units per thread, one fixed word per thread");
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 
 // instruction descriptor: D f32, A f16 (K-major), B f16 (MN-major), N = 192, M = 128
 constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
@@ -170,18 +182,24 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t bars = base + OFF_BAR;
   auto bar_full_tma = [&](int s) { return bars + 8u * s; };
-  auto bar_full_b = [&](int s) { return bars + 8u * (STAGES + s); };
-  auto bar_empty = [&](int s) { return bars + 8u * (2 * STAGES + s); };
-  auto bar_acc_full = [&](int a) { return bars + 8u * (3 * STAGES + a); };
-  auto bar_acc_empty = [&](int a) { return bars + 8u * (3 * STAGES + 2 + a); };
-  const uint32_t bar_done = bars + 8u * (3 * STAGES + 4);
+  auto bar_empty = [&](int s) { return bars + 8u * (STAGES + s); };
+  auto bar_bfull = [&](int j) { return bars + 8u * (2 * STAGES + j); };
+  auto bar_bempty = [&](int j) { return bars + 8u * (2 * STAGES + BSTAGES + j); };
+  auto bar_acc_full = [&](int a) { return bars + 8u * (2 * STAGES + 2 * BSTAGES + a); };
+  auto bar_acc_empty = [&](int a) { return bars + 8u * (2 * STAGES + 2 * BSTAGES + 2 + a); };
+  const uint32_t bar_done = bars + 8u * (2 * STAGES + 2 * BSTAGES + 4);
+  auto bar_conv = [&](int s) { return bars + 8u * (2 * STAGES + 2 * BSTAGES + 5 + s); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_TMEM);
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar_full_tma(s), 1);
-      mbar_init(bar_full_b(s), DQ_WARPS);
       mbar_init(bar_empty(s), 1);
+      mbar_init(bar_conv(s), 1);
+    }
+    for (int j = 0; j < BSTAGES; ++j) {
+      mbar_init(bar_bfull(j), DQ_WARPS);
+      mbar_init(bar_bempty(j), 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_acc_full(a), 1);
@@ -241,8 +259,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == WARP_MMA) {
     // ---- MMA issuer: one thread, accumulators in TMEM (two buffers)
     if (lane == 0) {
-      int stage = 0, acc = 0;
-      uint32_t ph = 0, aph = 0;
+      int stage = 0, acc = 0, bj = 0;
+      uint32_t ph = 0, aph = 0, bph = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
         const int tile = it / p.nnt;
@@ -253,20 +271,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc) * ACC_COLS;
         for (int kt = 0; kt < KT; ++kt) {
-          if (!mbar_wait(bar_full_tma(stage), ph) || !mbar_wait(bar_full_b(stage), ph)) {
+          if (!mbar_wait(bar_full_tma(stage), ph) || !mbar_wait(bar_bfull(bj), bph)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = base + OFF_A + stage * A_BYTES, b0 = base + OFF_B + stage * B_BYTES;
+          const uint32_t a0 = base + OFF_A + stage * A_BYTES, b0 = base + OFF_B + bj * B_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             umma_f16(d, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 2048, B_LBO, 1024),
                      (kt | kk) ? 1u : 0u);
-          umma_commit(bar_empty(stage));                   // frees the stage when these MMAs finish
+          umma_commit(bar_empty(stage));                   // frees the A / W stage when these MMAs finish
+          umma_commit(bar_bempty(bj));                     // and the B buffer
           if (++stage == STAGES) {
             stage = 0;
             ph ^= 1u;
+          }
+          if (++bj == BSTAGES) {
+            bj = 0;
+            bph ^= 1u;
           }
         }
         if (!ok) break;
@@ -324,9 +347,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(bar_done);
-  } else {
-    // ---- dequantisation: packed rows -> fp16 B tile, MN-major, 128-byte swizzle
-    const int d = tid - WARP_DQ0 * 32;                      // 0 .. 255
+  } else if (warp == WARP_CONV) {
+    // ---- scales / biases of each stage -> fp16 pairs (n, n+4) in the dequant's order
     int stage = 0;
     uint32_t ph = 0;
     bool ok = true;
@@ -336,41 +358,89 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (e < 0) continue;
       const int KT = (e >= p.E) ? GFS : GF;
       for (int kt = 0; kt < KT; ++kt) {
+        // (the stage's previous fp16 pairs were read before its previous MMAs, which came
+        // before the producer refilled it: the full barrier alone orders the overwrite)
         if (!mbar_wait(bar_full_tma(stage), ph)) {
           ok = false;
           break;
         }
-        const uint32_t* wr = reinterpret_cast<const uint32_t*>(gbase + OFF_W + stage * W_BYTES);
         const uint32_t* sb = reinterpret_cast<const uint32_t*>(gbase + OFF_SB + stage * SB_BYTES);
-        unsigned char* bt = gbase + OFF_B + stage * B_BYTES;
-#pragma unroll
-        for (int i = 0; i < BK * WPB / (DQ_WARPS * 32); ++i) {
-          const int u = d + DQ_WARPS * 32 * i;
-          const int k = u / WPB, w = u - k * WPB;          // neuron row k, word w of the block
-          const uint32_t qw = wr[k * WPB + w];
-          const uint4 s4 = *reinterpret_cast<const uint4*>(sb + w * 4);
-          const uint4 b4 = *reinterpret_cast<const uint4*>(sb + BN / 2 + w * 4);
-          const uint32_t sv[4] = {s4.x, s4.y, s4.z, s4.w};
-          const uint32_t bv[4] = {b4.x, b4.y, b4.z, b4.w};
-          uint32_t o[4];
-#pragma unroll
-          for (int pi = 0; pi < 4; ++pi) {                  // outputs 2pi, 2pi+1 of the word
-            const uint32_t t = qw >> (8 * pi);
-            const uint32_t x = (t & 0xFu) | ((t << 12) & 0xF0000u) | 0x64006400u;   // 1024 + q, exact
-            const __half2 qh = __hsub2(u32_as_h2(x), u32_as_h2(0x64006400u));
-            o[pi] = h2_as_u32(__hfma2(qh, u32_as_h2(pair_to_h2<ST>(sv[pi])), u32_as_h2(pair_to_h2<ST>(bv[pi]))));
-          }
-          const uint32_t off = static_cast<uint32_t>(w >> 3) * B_LBO + static_cast<uint32_t>(k >> 3) * 1024u +
-                               static_cast<uint32_t>(k & 7) * 128u +
-                               (static_cast<uint32_t>((w & 7) ^ (k & 7)) << 4);
-          *reinterpret_cast<uint4*>(bt + off) = make_uint4(o[0], o[1], o[2], o[3]);
+        uint32_t* sbh = reinterpret_cast<uint32_t*>(gbase + OFF_SBH + stage * SB_BYTES);
+        for (int t = lane; t < 2 * WPB; t += 32) {          // t < 24: scales of word t, else biases
+          const int wd = t % WPB, which = t / WPB;
+          const uint32_t* src = sb + which * (BN / 2) + wd * 4;   // 8 values of word wd: (0,1)(2,3)(4,5)(6,7)
+          uint32_t* dst = sbh + which * (BN / 2) + wd * 4;          // pairs (0,4)(1,5)(2,6)(3,7)
+          const uint32_t a = src[0], b = src[1], c = src[2], dd = src[3];
+          dst[0] = pair_to_h2<ST>(__byte_perm(a, c, 0x5410));
+          dst[1] = pair_to_h2<ST>(__byte_perm(a, c, 0x7632));
+          dst[2] = pair_to_h2<ST>(__byte_perm(b, dd, 0x5410));
+          dst[3] = pair_to_h2<ST>(__byte_perm(b, dd, 0x7632));
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor core reads
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar_full_b(stage));
+        if (lane == 0) mbar_arrive(bar_conv(stage));
         if (++stage == STAGES) {
           stage = 0;
           ph ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ---- dequantisation: packed rows -> fp16 B tile, MN-major, 128-byte swizzle.
+    // Thread d owns word w = d % 24 of every row it touches (rows k0, k0+16, k0+32, k0+48,
+    // k0 = d / 24), so its 8 scales and 8 biases are read once per K-tile. A word's nibbles
+    // become fp16 pairs (n, n+4) with one mask-and-or each (1024 + q, exact), minus 1024,
+    // times the pair's scales plus biases (one fp16 rounding), then byte permutes restore
+    // output order.
+    const int d = tid - WARP_DQ0 * 32;                      // 0 .. DQ_THREADS-1
+    const int w = d % WPB, k0 = d / WPB;
+    int stage = 0, bj = 0;
+    uint32_t ph = 0, bph = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+      const int tile = it / p.nnt;
+      const int e = p.tile_e[tile];
+      if (e < 0) continue;
+      const int KT = (e >= p.E) ? GFS : GF;
+      for (int kt = 0; kt < KT; ++kt) {
+        if (!mbar_wait(bar_full_tma(stage), ph) || !mbar_wait(bar_conv(stage), ph) ||
+            !mbar_wait(bar_bempty(bj), bph ^ 1u)) {
+          ok = false;
+          break;
+        }
+        const uint32_t* wr = reinterpret_cast<const uint32_t*>(gbase + OFF_W + stage * W_BYTES);
+        const uint32_t* sbh = reinterpret_cast<const uint32_t*>(gbase + OFF_SBH + stage * SB_BYTES);
+        unsigned char* bt = gbase + OFF_B + bj * B_BYTES;
+        const uint4 s4 = *reinterpret_cast<const uint4*>(sbh + w * 4);
+        const uint4 b4 = *reinterpret_cast<const uint4*>(sbh + BN / 2 + w * 4);
+#pragma unroll
+        for (int i = 0; i < BK / (DQ_THREADS / WPB); ++i) {
+          const int k = k0 + (DQ_THREADS / WPB) * i;       // neuron row of the K-tile
+          const uint32_t qw = wr[k * WPB + w];
+          const __half2 m1024 = u32_as_h2(0x64006400u);
+          const __half2 v0 = __hfma2(__hsub2(u32_as_h2((qw & 0x000F000Fu) | 0x64006400u), m1024), u32_as_h2(s4.x), u32_as_h2(b4.x));
+          const __half2 v1 = __hfma2(__hsub2(u32_as_h2(((qw >> 4) & 0x000F000Fu) | 0x64006400u), m1024), u32_as_h2(s4.y), u32_as_h2(b4.y));
+          const __half2 v2 = __hfma2(__hsub2(u32_as_h2(((qw >> 8) & 0x000F000Fu) | 0x64006400u), m1024), u32_as_h2(s4.z), u32_as_h2(b4.z));
+          const __half2 v3 = __hfma2(__hsub2(u32_as_h2(((qw >> 12) & 0x000F000Fu) | 0x64006400u), m1024), u32_as_h2(s4.w), u32_as_h2(b4.w));
+          // v_j = outputs (j, j+4): outputs (0,1), (2,3), (4,5), (6,7)
+          const uint32_t o0 = __byte_perm(h2_as_u32(v0), h2_as_u32(v1), 0x5410);
+          const uint32_t o1 = __byte_perm(h2_as_u32(v2), h2_as_u32(v3), 0x5410);
+          const uint32_t o2 = __byte_perm(h2_as_u32(v0), h2_as_u32(v1), 0x7632);
+          const uint32_t o3 = __byte_perm(h2_as_u32(v2), h2_as_u32(v3), 0x7632);
+          const uint32_t off = static_cast<uint32_t>(w >> 3) * B_LBO + static_cast<uint32_t>(k >> 3) * 1024u +
+                               static_cast<uint32_t>(k & 7) * 128u +
+                               (static_cast<uint32_t>((w & 7) ^ (k & 7)) << 4);
+          *reinterpret_cast<uint4*>(bt + off) = make_uint4(o0, o1, o2, o3);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor core reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_bfull(bj));
+        if (++stage == STAGES) {
+          stage = 0;
+          ph ^= 1u;
+        }
+        if (++bj == BSTAGES) {
+          bj = 0;
+          bph ^= 1u;
         }
       }
     }
