@@ -355,6 +355,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--only-prefill", action="store_true", help="profiling: the prefill leg alone")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--layers", type=int, default=23, help="fewer layers: small profiling case only")
     args = ap.parse_args()
@@ -405,6 +406,12 @@ def main():
         return
 
     layers = make_layers(device)
+    if args.only_prefill:
+        print(json.dumps({"prefill": prefill_leg(layers, device, dist_on, reps=steps)}), flush=True)
+        if dist_on:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
     wl = DecodeWorkload(layers, 1, 0.90, device, seed=1)
     wl.capture()
     with ClockSampler(device.index) as clk:
