@@ -145,6 +145,37 @@ int hsd_sparse_down_prefill(const void* h, int h_dtype, const float* gains, cons
                             int F, int FS, int topk, int E, void* workspace, size_t workspace_bytes,
                             void* stream);
 
+/* ---- Mamba-2 verify / rollback: hsd/mamba.py ------------------------------------- */
+
+/* The causal-conv half of hsd/mamba.py:28-32 (mamba_verify): window = [conv_state; conv_in]
+ * (K-1+L rows, conv_state NULL = zeros) is copied to `padded` (conv_in's dtype) and
+ * out[t, c] = silu(bias[c] + sum_j w[c, j] * window[t + j, c]) in fp32. conv_in rows are
+ * in_stride elements apart (a slice of the in_proj output). 1 <= L <= 64, K <= 8.
+ * in_dtype f32 / bf16, w_dtype f32 / bf16, out_dtype f32 / f16 / bf16. */
+int hsd_mamba_conv_verify(const void* conv_in, int in_dtype, int64_t in_stride,
+                          const void* conv_state, const void* w, int w_dtype, const void* bias,
+                          void* out, int out_dtype, void* padded, int L, int C, int K, void* stream);
+
+/* The SSM half of hsd/mamba.py:33-41 (mamba_verify with mlx-lm's ssm_update) for L rows:
+ *   xbc [L, >= H*P + 2*G*N] (x | B | C per row, x_dtype f32 / bf16, rows xbc_stride apart),
+ *   dt [L, >= H] (dt_dtype f32 / bf16, rows dt_stride apart), A_log / D / dt_bias [H] f32,
+ *   state0 [H, P, N] f32 (NULL = zeros) -> y [L, H*P] (y_dtype f32 / bf16) and
+ *   states [L, H, P, N] f32: the state after every row (the per-row checkpoints).
+ * dt_t = clamp(softplus(dt + dt_bias), dt_min, dt_max). Rows run as single steps would, so
+ * states[n-1] equals n single steps bit for bit. N in {32, 64, 128, 256}, H % G == 0. */
+int hsd_mamba_ssm_verify(const void* xbc, int x_dtype, int64_t xbc_stride, const void* dt,
+                         int dt_dtype, int64_t dt_stride, const float* A_log, const float* D,
+                         const float* dt_bias, float dt_min, float dt_max, const float* state0,
+                         float* states, void* y, int y_dtype, int L, int H, int P, int G, int N,
+                         void* stream);
+
+/* hsd/mamba.py:47 mamba_rollback(records, n_keep), on device and without recomputation:
+ * state_out = states[n_keep-1], conv_out = padded[n_keep : n_keep+K-1] (elem_bytes per
+ * element). 1 <= n_keep <= L. */
+int hsd_mamba_rollback(const float* states, const void* padded, int elem_bytes, int n_keep, int L,
+                       int H, int P, int N, int C, int K, float* state_out, void* conv_out,
+                       void* stream);
+
 /* ---- allocation-free prefill ------------------------------------------------------ */
 
 /* No counterpart in the reference. For callers that cannot call cudaMalloc (code running

@@ -1,0 +1,210 @@
+// Mamba-2 multi-row verify with per-row checkpointed state, and the rollback to an accepted
+// prefix (hsd/mamba.py:19-56 of the reference, which records the verify's inputs and re-runs
+// mlx-lm's ssm_update over the kept rows; here every row's state is written once during the
+// verify, so a rollback is a selection and never a recomputation).
+//
+// conv_verify  one thread per channel: the window [conv_state; conv_in] (K-1+L rows) is
+//              copied to `padded` and out[t] = silu(bias + sum_j w[c, j] * padded[t + j]) in
+//              fp32. After keeping n rows the conv state is padded[n : n+K-1].
+// ssm_verify   one warp per (head h, channel p); lane l holds state[h, p, l*NPL .. +NPL) in
+//              registers. Rows one after another, exactly as single steps would run them:
+//                dt_t = clamp(softplus(dt[t,h] + dt_bias[h]), dt_min, dt_max)
+//                state = state * exp(dt_t * A_h) + (dt_t * x[t,h,p]) * B[t, g(h), :]
+//                y[t,h,p] = sum_n state * C[t, g(h), :] + D_h * x[t,h,p]   (warp reduction)
+//              and after every row the warp stores its state slice to states[t] (coalesced).
+//              A verify of L rows and L single steps run the same instructions per row, so
+//              the state after row n of a verify is bit-identical to n single steps.
+#include "hsd_common.cuh"
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld(const void* p, int64_t i) {
+  return hsd::to_f32<T>(reinterpret_cast<const T*>(p)[i]);
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+
+template <typename TI, typename TW, typename TO>
+__global__ void __launch_bounds__(256) conv_verify_kernel(const void* conv_in, int64_t in_stride,
+                                                          const void* conv_state, const void* w,
+                                                          const void* bias, void* out, void* padded, int L,
+                                                          int C, int K) {
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c >= C) return;
+  float win[8 + 64];                               // K-1 + L <= 71 (checked on the host)
+  const int NW = K - 1 + L;
+  for (int j = 0; j < K - 1; ++j) win[j] = conv_state ? ld<TI>(conv_state, static_cast<int64_t>(j) * C + c) : 0.f;
+  for (int t = 0; t < L; ++t) win[K - 1 + t] = ld<TI>(conv_in, static_cast<int64_t>(t) * in_stride + c);
+  for (int j = 0; j < NW; ++j)
+    reinterpret_cast<TI*>(padded)[static_cast<int64_t>(j) * C + c] = hsd::from_f32<TI>(win[j]);
+  const float b = bias ? ld<TW>(bias, c) : 0.f;
+  float wk[8];
+  for (int j = 0; j < K; ++j) wk[j] = ld<TW>(w, static_cast<int64_t>(c) * K + j);
+  for (int t = 0; t < L; ++t) {
+    float a = b;
+    for (int j = 0; j < K; ++j) a = fmaf(wk[j], win[t + j], a);
+    reinterpret_cast<TO*>(out)[static_cast<int64_t>(t) * C + c] = hsd::from_f32<TO>(silu_f(a));
+  }
+}
+
+template <typename TX, typename TD, typename TY, int NPL>
+__global__ void __launch_bounds__(256) ssm_verify_kernel(const void* xbc, int64_t xbc_stride, const void* dt,
+                                                         int64_t dt_stride, const float* __restrict__ A_log,
+                                                         const float* __restrict__ Dp,
+                                                         const float* __restrict__ dt_bias, float dt_min,
+                                                         float dt_max, const float* __restrict__ state0,
+                                                         float* __restrict__ states, void* y, int L, int H, int P,
+                                                         int G, int N) {
+  const int warp_g = (blockIdx.x * 256 + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_g >= H * P) return;
+  const int h = warp_g / P, p = warp_g - h * P;
+  const int g = h / (H / G);
+  const int I = H * P;
+  const int64_t sbase = (static_cast<int64_t>(h) * P + p) * N + lane * NPL;   // this lane's slice
+  float st[NPL];
+#pragma unroll
+  for (int i = 0; i < NPL; ++i) st[i] = state0 ? state0[sbase + i] : 0.f;
+  const float A = -expf(A_log[h]);
+  const float dbias = dt_bias[h], Dh = Dp[h];
+  for (int t = 0; t < L; ++t) {
+    const int64_t row = static_cast<int64_t>(t) * xbc_stride;
+    const float x = ld<TX>(xbc, row + static_cast<int64_t>(h) * P + p);
+    const float dtt = fminf(fmaxf(softplus_f(ld<TD>(dt, static_cast<int64_t>(t) * dt_stride + h) + dbias), dt_min), dt_max);
+    const float dA = expf(dtt * A);
+    const float dx = dtt * x;
+    const int64_t bo = row + I + static_cast<int64_t>(g) * N + lane * NPL;
+    const int64_t co = row + I + static_cast<int64_t>(G) * N + static_cast<int64_t>(g) * N + lane * NPL;
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) {
+      st[i] = fmaf(st[i], dA, dx * ld<TX>(xbc, bo + i));
+      acc = fmaf(st[i], ld<TX>(xbc, co + i), acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0)
+      reinterpret_cast<TY*>(y)[static_cast<int64_t>(t) * I + static_cast<int64_t>(h) * P + p] =
+          hsd::from_f32<TY>(fmaf(Dh, x, acc));
+    float* dst = states + static_cast<int64_t>(t) * H * P * N + sbase;
+    if constexpr (NPL % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < NPL; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(st[i], st[i + 1], st[i + 2], st[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) dst[i] = st[i];
+    }
+  }
+}
+
+template <typename TI, typename TW>
+int conv_dispatch_out(int out_dtype, dim3 grid, cudaStream_t st, const void* conv_in, int64_t in_stride,
+                      const void* conv_state, const void* w, const void* bias, void* out, void* padded, int L, int C,
+                      int K) {
+  switch (out_dtype) {
+    case HSD_F32: conv_verify_kernel<TI, TW, float><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K); break;
+    case HSD_F16: conv_verify_kernel<TI, TW, __half><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K); break;
+    case HSD_BF16: conv_verify_kernel<TI, TW, __nv_bfloat16><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K); break;
+    default: return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_conv_verify: out_dtype %d", out_dtype);
+  }
+  return hsd::check_launch("hsd_mamba_conv_verify");
+}
+
+template <typename TI>
+int conv_dispatch_w(int w_dtype, int out_dtype, dim3 grid, cudaStream_t st, const void* conv_in, int64_t in_stride,
+                    const void* conv_state, const void* w, const void* bias, void* out, void* padded, int L, int C,
+                    int K) {
+  switch (w_dtype) {
+    case HSD_F32: return conv_dispatch_out<TI, float>(out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K);
+    case HSD_BF16: return conv_dispatch_out<TI, __nv_bfloat16>(out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K);
+  }
+  return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_conv_verify: w_dtype %d (f32 or bf16)", w_dtype);
+}
+
+template <typename TX, typename TD, typename TY>
+int ssm_dispatch_n(int N, dim3 grid, cudaStream_t st, const void* xbc, int64_t xbc_stride, const void* dt,
+                   int64_t dt_stride, const float* A_log, const float* Dp, const float* dt_bias, float dt_min,
+                   float dt_max, const float* state0, float* states, void* y, int L, int H, int P, int G) {
+  switch (N) {
+    case 32: ssm_verify_kernel<TX, TD, TY, 1><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N); break;
+    case 64: ssm_verify_kernel<TX, TD, TY, 2><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N); break;
+    case 128: ssm_verify_kernel<TX, TD, TY, 4><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N); break;
+    case 256: ssm_verify_kernel<TX, TD, TY, 8><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N); break;
+    default: return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_ssm_verify: N must be 32, 64, 128 or 256 (got %d)", N);
+  }
+  return hsd::check_launch("hsd_mamba_ssm_verify");
+}
+
+template <typename TX>
+int ssm_dispatch(int dt_dtype, int y_dtype, int N, dim3 grid, cudaStream_t st, const void* xbc, int64_t xbc_stride,
+                 const void* dt, int64_t dt_stride, const float* A_log, const float* Dp, const float* dt_bias,
+                 float dt_min, float dt_max, const float* state0, float* states, void* y, int L, int H, int P,
+                 int G) {
+#define HSD_SSM_Y(TD)                                                                                            \
+  switch (y_dtype) {                                                                                           \
+    case HSD_F32: return ssm_dispatch_n<TX, TD, float>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G); \
+    case HSD_BF16: return ssm_dispatch_n<TX, TD, __nv_bfloat16>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G); \
+  }                                                                                                            \
+  return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_ssm_verify: y_dtype %d (f32 or bf16)", y_dtype);
+  switch (dt_dtype) {
+    case HSD_F32: { HSD_SSM_Y(float) }
+    case HSD_BF16: { HSD_SSM_Y(__nv_bfloat16) }
+  }
+#undef HSD_SSM_Y
+  return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_ssm_verify: dt_dtype %d (f32 or bf16)", dt_dtype);
+}
+
+}  // namespace
+
+extern "C" int hsd_mamba_conv_verify(const void* conv_in, int in_dtype, int64_t in_stride, const void* conv_state,
+                                     const void* w, int w_dtype, const void* bias, void* out, int out_dtype,
+                                     void* padded, int L, int C, int K, void* stream) {
+  if (!conv_in || !w || !out || !padded) return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_conv_verify: null pointer");
+  if (L < 1 || L > 64 || C < 1 || K < 1 || K > 8 || in_stride < C)
+    return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_conv_verify: need 1 <= L <= 64, 1 <= K <= 8, in_stride >= C");
+  dim3 grid((C + 255) / 256);
+  cudaStream_t st = hsd::as_stream(stream);
+  switch (in_dtype) {
+    case HSD_F32: return conv_dispatch_w<float>(w_dtype, out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K);
+    case HSD_BF16: return conv_dispatch_w<__nv_bfloat16>(w_dtype, out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K);
+  }
+  return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_conv_verify: in_dtype %d (f32 or bf16)", in_dtype);
+}
+
+extern "C" int hsd_mamba_ssm_verify(const void* xbc, int x_dtype, int64_t xbc_stride, const void* dt, int dt_dtype,
+                                    int64_t dt_stride, const float* A_log, const float* D, const float* dt_bias,
+                                    float dt_min, float dt_max, const float* state0, float* states, void* y,
+                                    int y_dtype, int L, int H, int P, int G, int N, void* stream) {
+  if (!xbc || !dt || !A_log || !D || !dt_bias || !states || !y)
+    return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_ssm_verify: null pointer");
+  if (L < 1 || H < 1 || P < 1 || G < 1 || H % G != 0 || xbc_stride < static_cast<int64_t>(H) * P + 2 * G * N)
+    return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_ssm_verify: bad shape (H %% G == 0, xbc_stride >= H*P + 2*G*N)");
+  if (!hsd::aligned(states, 16) || (state0 && !hsd::aligned(state0, 16)))
+    return hsd::set_error(HSD_ERR_ALIGN, "hsd_mamba_ssm_verify: states must be 16-byte aligned");
+  const int64_t warps = static_cast<int64_t>(H) * P;
+  dim3 grid(static_cast<unsigned>((warps * 32 + 255) / 256));
+  cudaStream_t st = hsd::as_stream(stream);
+  switch (x_dtype) {
+    case HSD_F32: return ssm_dispatch<float>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G);
+    case HSD_BF16: return ssm_dispatch<__nv_bfloat16>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G);
+  }
+  return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_ssm_verify: x_dtype %d (f32 or bf16)", x_dtype);
+}
+
+extern "C" int hsd_mamba_rollback(const float* states, const void* padded, int elem_bytes, int n_keep, int L, int H,
+                                  int P, int N, int C, int K, float* state_out, void* conv_out, void* stream) {
+  if (!states || !padded || !state_out || !conv_out) return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_rollback: null pointer");
+  if (n_keep < 1 || n_keep > L || elem_bytes < 1 || K < 1)
+    return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_rollback: need 1 <= n_keep <= L (got n_keep=%d L=%d)", n_keep, L);
+  cudaStream_t st = hsd::as_stream(stream);
+  const size_t sbytes = static_cast<size_t>(H) * P * N * sizeof(float);
+  cudaError_t e = cudaMemcpyAsync(state_out, states + static_cast<size_t>(n_keep - 1) * H * P * N, sbytes,
+                                  cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return hsd::check_cuda(e, "hsd_mamba_rollback: state copy");
+  const size_t cbytes = static_cast<size_t>(K - 1) * C * elem_bytes;
+  e = cudaMemcpyAsync(conv_out, static_cast<const char*>(padded) + static_cast<size_t>(n_keep) * C * elem_bytes, cbytes,
+                      cudaMemcpyDeviceToDevice, st);
+  return hsd::check_cuda(e, "hsd_mamba_rollback: conv window copy");
+}
