@@ -332,6 +332,32 @@ def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512):
                     "dense_equiv = 2*T*(6F+FS)*D"}
 
 
+def ep_leg(layers, device, dist_on, reps=10):
+    """Expert-parallel MoE down projection across the ranks (layer 0's experts sharded E/G per
+    GPU, tokens on their home rank): batch decode B = 64 and a prefill chunk of 512 tokens per
+    rank (weak scaling), NCCL all-to-all dispatch / combine around this library's kernels.
+    -> dict of tokens/s summed over ranks (device time, max over ranks)."""
+    import torch.distributed as dist
+    from hsd_b200.ep import ExpertParallelDown
+    world, rank = dist.get_world_size(), dist.get_rank()
+    EL = E // world
+    pw, ps, pb, spw, sps, spb = layers[0]
+    ep = ExpertParallelDown(E, F, FS, D, TOPK, pw[rank * EL:(rank + 1) * EL].contiguous(),
+                            ps[rank * EL:(rank + 1) * EL].contiguous(), pb[rank * EL:(rank + 1) * EL].contiguous(),
+                            spw, sps, spb)
+    out = {}
+    for name, T in (("batch_decode_B64", 64), ("prefill_chunk_512", 512)):
+        gen = torch.Generator(device=device).manual_seed(100 + rank)
+        sel, sc = synth.route_zipf(T, E, TOPK, gen, device)
+        gains = torch.cat([sc, torch.ones((T, 1), device=device)], 1).contiguous()
+        h = synth.relu2_activations((T, TOPK * F + FS), 0.90, gen, device)
+        ms = timed(lambda _: ep(h, sel, gains), reps, 3, device, dist_on) / reps
+        out[name] = {"ms": ms, "tokens_per_s_all_ranks": world * T / (ms / 1e3)}
+    out["gpus"] = world
+    out["note"] = "experts 0..127 split 128/G per GPU; slots exchanged with NCCL all_to_all_single"
+    return out
+
+
 def traffic_from_profile():
     """Per-launch DRAM traffic of the decode kernel from the committed ncu summary."""
     p = os.path.join(REPO, "profiles", "decode_sparse_down_ncu.md")
@@ -443,6 +469,7 @@ def main():
     prefill = None
     if not args.no_prefill:
         prefill = prefill_leg(layers, device, dist_on)
+    ep = ep_leg(layers, device, dist_on) if dist_on else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -470,6 +497,7 @@ def main():
         "us_per_layer": launch_ms * 1e3,
         "sweep": sweep,
         "prefill": prefill,
+        "expert_parallel": ep,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -87,6 +87,9 @@ int hsd_swap_last2_u16(const uint16_t* in, uint16_t* out, int64_t lead, int64_t 
  * Reads only the weight rows of nonzero h entries and the scales / biases of 64-neuron
  * groups with at least one nonzero entry. loadsc = 0 is the reference's benchmark-only
  * switch (hsd/decode.py:25-27) that skips the scale / bias loads.
+ * topk = 0 (the shared expert alone; sel / pw / ps / pb may be NULL, gains [B, 1]) and FS = 0
+ * (routed experts alone; spw / sps / spb may be NULL) are the per-slot forms the
+ * expert-parallel exchange uses.
  * Supported: D % 32 == 0, F % 64 == 0, FS % 64 == 0, 1 <= B <= 65535; h, pw, ps, pb, spw,
  * sps and spb 16-byte aligned (HSD_ERR_ALIGN otherwise). Launched with programmatic
  * dependent launch: it waits for the previous kernel in the stream before reading. */

@@ -527,13 +527,19 @@ extern "C" int hsd_sparse_down_decode(const void* h, int h_dtype, const int32_t*
                                       const void* sps, const void* spb, const void* resid, void* y,
                                       int y_dtype, int B, int D, int F, int FS, int topk, int E,
                                       int loadsc, void* stream) {
-  if (!h || !sel || !gains || !pw || !ps || !pb || !spw || !sps || !spb || !y)
-    return hsd::set_error(HSD_ERR_ARG, "hsd_sparse_down_decode: null pointer");
-  if (B < 1 || B > 65535 || D < 32 || D % 32 != 0 || F < 64 || F % 64 != 0 || FS < 64 ||
-      FS % 64 != 0 || topk < 1 || E < 1)
+  // topk == 0: the shared expert alone; FS == 0: routed experts alone (the forms the
+  // expert-parallel exchange uses); the pointers of an absent part may be NULL
+  if (!h || !gains || !y) return hsd::set_error(HSD_ERR_ARG, "hsd_sparse_down_decode: null pointer");
+  if (topk > 0 && (!sel || !pw || !ps || !pb))
+    return hsd::set_error(HSD_ERR_ARG, "hsd_sparse_down_decode: null routed-expert pointer");
+  if (FS > 0 && (!spw || !sps || !spb))
+    return hsd::set_error(HSD_ERR_ARG, "hsd_sparse_down_decode: null shared-expert pointer");
+  if (topk == 0) F = 64;                         // no routed columns: F is unused
+  if (B < 1 || B > 65535 || D < 32 || D % 32 != 0 || F < 64 || F % 64 != 0 || FS < 0 ||
+      FS % 64 != 0 || topk < 0 || (topk > 0 && E < 1) || (topk == 0 && FS == 0))
     return hsd::set_error(HSD_ERR_SHAPE,
                           "hsd_sparse_down_decode: need 1<=B<=65535, D%%32==0, F%%64==0, FS%%64==0, "
-                          "topk>=1, E>=1 (got B=%d D=%d F=%d FS=%d topk=%d E=%d)",
+                          "topk>=0, E>=1 when topk>0, topk*F+FS>0 (got B=%d D=%d F=%d FS=%d topk=%d E=%d)",
                           B, D, F, FS, topk, E);
   const long long NR = static_cast<long long>(topk) * F + FS;
   if (NR > (1ll << 30) || static_cast<long long>(E) * F * (D / 8) > (1ll << 40))

@@ -190,13 +190,13 @@ __global__ void __launch_bounds__(256) gather_kernel(const HT* __restrict__ h,
 // y[t, o] = sum_{p = 0..topk} part[t*(topk+1) + p, o] (+ resid), fixed order.
 template <typename YT>
 __global__ void __launch_bounds__(256) partial_reduce_kernel(const float* __restrict__ part, const void* resid,
-                                                     void* y, int T, int D, int topk) {
+                                                     void* y, int T, int D, int topk, int nparts) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
   if (i >= static_cast<int64_t>(T) * D) return;
   const int64_t t = i / D, o = i - t * D;
   const float* p = part + t * (topk + 1) * static_cast<int64_t>(D) + o;
   float acc = 0.f;
-  for (int k = 0; k <= topk; ++k) acc += p[static_cast<int64_t>(k) * D];
+  for (int k = 0; k < nparts; ++k) acc += p[static_cast<int64_t>(k) * D];   // (no shared row when FS == 0)
   if (resid) acc += hsd::to_f32<YT>(reinterpret_cast<const YT*>(resid)[i]);
   reinterpret_cast<YT*>(y)[i] = hsd::from_f32<YT>(acc);
 }
@@ -242,13 +242,13 @@ int launch_gather(const void* h, int h_dtype, const int32_t* tile_e, const int32
 }
 
 int launch_reduce(const float* part, const void* resid, void* y, int y_dtype, int T, int D, int topk,
-                  cudaStream_t st) {
+                  int nparts, cudaStream_t st) {
   const int64_t n = static_cast<int64_t>(T) * D;
   const unsigned grid = static_cast<unsigned>((n + 255) / 256);
   switch (y_dtype) {
-    case HSD_F32: partial_reduce_kernel<float><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk); break;
-    case HSD_F16: partial_reduce_kernel<__half><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk); break;
-    case HSD_BF16: partial_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk); break;
+    case HSD_F32: partial_reduce_kernel<float><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk, nparts); break;
+    case HSD_F16: partial_reduce_kernel<__half><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk, nparts); break;
+    case HSD_BF16: partial_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(part, resid, y, T, D, topk, nparts); break;
     default: return set_error(HSD_ERR_DTYPE, "prefill reduce: y_dtype %d", y_dtype);
   }
   return check_launch("prefill reduce");
@@ -335,9 +335,10 @@ extern "C" int hsd_sparse_down_prefill(const void* h, int h_dtype, const float* 
                                        const void* spb, const void* resid, void* y, int y_dtype, int T, int D, int F,
                                        int FS, int topk, int E, void* workspace, size_t workspace_bytes,
                                        void* stream) {
-  if (!h || !gains || !tile_e || !tile_slot || !pw || !ps || !pb || !spw || !sps || !spb || !y || !workspace)
+  if (!h || !gains || !tile_e || !tile_slot || !pw || !ps || !pb || !y || !workspace ||
+      (FS > 0 && (!spw || !sps || !spb)))
     return hsd::set_error(HSD_ERR_ARG, "hsd_sparse_down_prefill: null pointer");
-  if (T < 1 || D < 192 || D % 192 != 0 || F < 64 || F % 64 != 0 || FS < 64 || FS % 64 != 0 || topk < 1 || E < 1)
+  if (T < 1 || D < 192 || D % 192 != 0 || F < 64 || F % 64 != 0 || FS < 0 || FS % 64 != 0 || topk < 1 || E < 1)
     return hsd::set_error(HSD_ERR_SHAPE,
                           "hsd_sparse_down_prefill: need D %% 192 == 0, F %% 64 == 0, FS %% 64 == 0 "
                           "(got T=%d D=%d F=%d FS=%d topk=%d E=%d)", T, D, F, FS, topk, E);
@@ -366,5 +367,5 @@ extern "C" int hsd_sparse_down_prefill(const void* h, int h_dtype, const float* 
   rc = hsd::launch_prefill_gemm(hc, kmax, tile_e, tile_slot, NT, gains, pw, ps, pb, s_dtype, spw, sps, spb, part, T, D,
                                 F, FS, topk, E, st);
   if (rc) return rc;
-  return hsd::launch_reduce(part, resid, y, y_dtype, T, D, topk, st);
+  return hsd::launch_reduce(part, resid, y, y_dtype, T, D, topk, topk + (FS > 0 ? 1 : 0), st);
 }

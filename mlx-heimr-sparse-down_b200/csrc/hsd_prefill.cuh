@@ -14,9 +14,9 @@ int prefill_tile_counts(int T, int topk, int E, int tt, int* nt_routed, int* nt_
 int launch_gather(const void* h, int h_dtype, const int32_t* tile_e, const int32_t* tile_slot, int NT,
                   int tt, int F, int FS, int topk, int E, int kmax, __half* hc, cudaStream_t st);
 
-// y[t] = sum over the token's topk + 1 partial rows (+ resid), fixed order.
+// y[t] = sum over the token's first nparts partial rows (+ resid), fixed order.
 int launch_reduce(const float* part, const void* resid, void* y, int y_dtype, int T, int D, int topk,
-                  cudaStream_t st);
+                  int nparts, cudaStream_t st);
 
 // The tensor-core grouped GEMM over the tile order (hsd_prefill_gemm.cu).
 int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const int32_t* tile_slot, int NT,

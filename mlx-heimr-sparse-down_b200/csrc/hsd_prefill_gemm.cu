@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int e = p.tile_e[tile];
         if (e < 0) continue;
         const bool shared = e >= p.E;
-        const int KT = shared ? GFS : GF;
+        const int KT = shared ? GFS : GF;              // 0 for shared tiles when FS == 0: skipped
         for (int kt = 0; kt < KT; ++kt) {
           if (!mbar_wait(bar_empty(stage), ph ^ 1u)) {
             ok = false;
@@ -267,6 +267,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int e = p.tile_e[tile];
         if (e < 0) continue;
         const int KT = (e >= p.E) ? GFS : GF;
+        if (KT == 0) continue;
         if (!mbar_wait(bar_acc_empty(acc), aph ^ 1u)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc) * ACC_COLS;
@@ -314,7 +315,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
       const int tile = it / p.nnt, nt = it - tile * p.nnt;
       const int e = p.tile_e[tile];
-      if (e < 0) continue;
+      if (e < 0 || ((e >= p.E) ? GFS : GF) == 0) continue;
       if (!mbar_wait(bar_acc_full(acc), aph)) break;
       tc_fence_after();
       const int s = p.tile_slot[static_cast<int64_t>(tile) * BM + m];
@@ -506,7 +507,7 @@ int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const
                         const float* gains, const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
                         const uint32_t* spw, const void* sps, const void* spb, float* part, int T, int D,
                         int F, int FS, int topk, int E, cudaStream_t st) {
-  if (D % BN != 0 || F % BK != 0 || FS % BK != 0 || kmax % BK != 0)
+  if (D % BN != 0 || F % BK != 0 || FS < 0 || FS % BK != 0 || kmax % BK != 0)
     return set_error(HSD_ERR_SHAPE, "prefill gemm: need D %% %d == 0, F and FS %% 64 == 0 (D=%d F=%d FS=%d)", BN,
                      D, F, FS);
   CUtensorMap ma, mw, mws;
@@ -518,8 +519,11 @@ int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const
                  static_cast<uint64_t>(E) * F, static_cast<uint64_t>(D / 8) * 4, WPB, BK, CU_TENSOR_MAP_SWIZZLE_NONE,
                  "W");
   if (rc) return rc;
-  rc = encode_2d(&mws, CU_TENSOR_MAP_DATA_TYPE_UINT32, spw, static_cast<uint64_t>(D / 8), static_cast<uint64_t>(FS),
-                 static_cast<uint64_t>(D / 8) * 4, WPB, BK, CU_TENSOR_MAP_SWIZZLE_NONE, "Ws");
+  // (with FS == 0 there are no shared tiles to load: the routed map stands in, unused)
+  rc = FS > 0 ? encode_2d(&mws, CU_TENSOR_MAP_DATA_TYPE_UINT32, spw, static_cast<uint64_t>(D / 8),
+                          static_cast<uint64_t>(FS), static_cast<uint64_t>(D / 8) * 4, WPB, BK,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, "Ws")
+              : (mws = mw, HSD_OK);
   if (rc) return rc;
   GemmParams p;
   p.tile_e = tile_e;

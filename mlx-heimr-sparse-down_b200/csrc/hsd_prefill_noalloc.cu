@@ -109,9 +109,9 @@ extern "C" int hsd_sparse_down_prefill_noalloc(const void* h, int h_dtype, const
                                                const uint32_t* spw, const void* sps, const void* spb,
                                                const void* resid, void* y, int y_dtype, int T, int D, int F, int FS,
                                                int topk, int E, void* stream) {
-  if (!h || !gains || !tile_e || !tile_slot || !pw || !ps || !pb || !spw || !sps || !spb || !y)
+  if (!h || !gains || !tile_e || !tile_slot || !pw || !ps || !pb || !y || (FS > 0 && (!spw || !sps || !spb)))
     return hsd::set_error(HSD_ERR_ARG, "hsd_sparse_down_prefill_noalloc: null pointer");
-  if (T < 1 || D < 192 || D % 192 != 0 || F < 64 || F % 64 != 0 || FS < 64 || FS % 64 != 0 || topk < 1 || E < 1)
+  if (T < 1 || D < 192 || D % 192 != 0 || F < 64 || F % 64 != 0 || FS < 0 || FS % 64 != 0 || topk < 1 || E < 1)
     return hsd::set_error(HSD_ERR_SHAPE,
                           "hsd_sparse_down_prefill_noalloc: need D %% 192 == 0, F %% 64 == 0, FS %% 64 == 0 "
                           "(got T=%d D=%d F=%d FS=%d topk=%d E=%d)", T, D, F, FS, topk, E);
@@ -149,5 +149,5 @@ extern "C" int hsd_sparse_down_prefill_noalloc(const void* h, int h_dtype, const
   rc = hsd::launch_prefill_gemm(hc, kmax, te_c, ts_c, L.NC, gains, pw, ps, pb, s_dtype, spw, sps, spb, part, T, D, F,
                                 FS, topk, E, st);
   if (rc) return rc;
-  return hsd::launch_reduce(part, resid, y, y_dtype, T, D, topk, st);
+  return hsd::launch_reduce(part, resid, y, y_dtype, T, D, topk, topk + (FS > 0 ? 1 : 0), st);
 }

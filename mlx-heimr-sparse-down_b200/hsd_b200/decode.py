@@ -28,23 +28,27 @@ def sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D, topk,
     del sl, unr, nds
     what = "sparse_down"
     _lib.require_cuda(h, sel, gains, pw, ps, pb, spw, sps, spb, resid, out, what=what)
-    if h.dim() != 2 or sel.dim() != 2 or gains.dim() != 2:
-        raise ValueError(f"{what}: h, sel, gains must be 2-D")
+    if h.dim() != 2 or gains.dim() != 2:
+        raise ValueError(f"{what}: h and gains must be 2-D")
     B = h.shape[0]
-    E = pw.shape[0]
+    E = pw.shape[0] if pw is not None else 0
     if h.shape[1] != topk * F + FS:
         raise ValueError(f"{what}: h has {h.shape[1]} columns, expected topk*F+FS = {topk * F + FS}")
-    if tuple(sel.shape) != (B, topk) or sel.dtype != torch.int32:
-        raise ValueError(f"{what}: sel must be int32 [{B}, {topk}] (got {sel.dtype} {tuple(sel.shape)})")
     if tuple(gains.shape) != (B, topk + 1) or gains.dtype != torch.float32:
         raise ValueError(f"{what}: gains must be float32 [{B}, {topk + 1}]")
-    if tuple(pw.shape) != (E, F, D // 8) or tuple(ps.shape) != (E, F // 64, D) or ps.shape != pb.shape:
-        raise ValueError(f"{what}: routed layout shapes {tuple(pw.shape)} {tuple(ps.shape)} {tuple(pb.shape)}"
-                         f" do not match E={E} F={F} D={D}")
-    if tuple(spw.shape) != (FS, D // 8) or tuple(sps.shape) != (FS // 64, D) or sps.shape != spb.shape:
-        raise ValueError(f"{what}: shared layout shapes do not match FS={FS} D={D}")
-    if ps.dtype != pb.dtype or sps.dtype != ps.dtype or spb.dtype != ps.dtype:
-        raise TypeError(f"{what}: scales and biases must share one 16-bit dtype")
+    if topk > 0:
+        if sel is None or tuple(sel.shape) != (B, topk) or sel.dtype != torch.int32:
+            raise ValueError(f"{what}: sel must be int32 [{B}, {topk}]")
+        if tuple(pw.shape) != (E, F, D // 8) or tuple(ps.shape) != (E, F // 64, D) or ps.shape != pb.shape:
+            raise ValueError(f"{what}: routed layout shapes {tuple(pw.shape)} {tuple(ps.shape)} {tuple(pb.shape)}"
+                             f" do not match E={E} F={F} D={D}")
+    if FS > 0:
+        if tuple(spw.shape) != (FS, D // 8) or tuple(sps.shape) != (FS // 64, D) or sps.shape != spb.shape:
+            raise ValueError(f"{what}: shared layout shapes do not match FS={FS} D={D}")
+    sref = ps if topk > 0 else sps
+    for t in (pb, sps, spb):
+        if t is not None and t.dtype != sref.dtype:
+            raise TypeError(f"{what}: scales and biases must share one 16-bit dtype")
     od = out_dtype or h.dtype
     if out is None:
         out = torch.empty((B, D), dtype=od, device=h.device)
@@ -55,7 +59,7 @@ def sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D, topk,
     if B == 0:
         return out
     _lib.call("hsd_sparse_down_decode", _lib.ptr(h), _lib.dtype_code(h, what), _lib.ptr(sel),
-              _lib.ptr(gains), _lib.ptr(pw), _lib.ptr(ps), _lib.ptr(pb), _lib.dtype_code(ps, what),
+              _lib.ptr(gains), _lib.ptr(pw), _lib.ptr(ps), _lib.ptr(pb), _lib.dtype_code(sref, what),
               _lib.ptr(spw), _lib.ptr(sps), _lib.ptr(spb), _lib.ptr(resid), _lib.ptr(out),
               _lib.dtype_code(out, what), B, D, F, FS, topk, E, 1 if loadsc else 0, _lib.stream_of(h))
     return out

@@ -1,0 +1,86 @@
+"""Expert-parallel dispatch / combine on CPU ranks (gloo, world size 2): the exchange logic of
+hsd_b200.ep with the oracle's arithmetic standing in for the kernels, against the single-process
+oracle. No GPU."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+D, F, FS, E, TOPK = 128, 128, 128, 8, 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _case():
+    from hsd_b200 import synth
+    return synth.decode_case(seed=3, B=12, D=D, F=F, FS=FS, E=E, topk=TOPK, zero_frac=0.7)
+
+
+def _worker(rank, world, port, tokens_per_rank, q):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    for pth in (os.path.join(os.path.dirname(here), "mlx-heimr-sparse-down_b200"), os.path.dirname(here), here):
+        sys.path.insert(0, pth)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import decode as od
+        from oracle import layout as ol
+        from oracle.quant import bf16_bits_to_f32, dequantize_neuron_major
+        from hsd_b200.ep import ExpertParallelDown
+        c = _case()
+        u16 = lambda t: t.view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        w = c["w"].numpy().view(np.uint32)
+        pw, ps, pb = ol.to_neuron_major(w, u16(c["s"]), u16(c["b"]))
+        Wt = dequantize_neuron_major(pw, bf16_bits_to_f32(ps), bf16_bits_to_f32(pb))       # [E, F, D]
+        spw, sps, spb = ol.to_neuron_major(c["sw"].numpy().view(np.uint32), u16(c["ss"]), u16(c["sb"]))
+        Wst = dequantize_neuron_major(spw, bf16_bits_to_f32(sps), bf16_bits_to_f32(spb))   # [FS, D]
+        E_local = E // world
+
+        def local_down(h, ids, g):          # the owner's arithmetic, oracle-side (fp32)
+            hf = h.float().numpy()
+            y = np.stack([g[r].item() * (hf[r] @ Wt[rank * E_local + int(ids[r])]) for r in range(h.shape[0])])
+            return torch.from_numpy(y.astype(np.float32))
+
+        def shared_down(hs, g):
+            return torch.from_numpy((hs.float().numpy() @ Wst).astype(np.float32)) * g
+
+        ep = ExpertParallelDown(E, F, FS, D, TOPK, group=None, local_down=local_down, shared_down=shared_down)
+        lo = sum(tokens_per_rank[:rank])
+        hi = lo + tokens_per_rank[rank]
+        y = ep(c["h"][lo:hi], c["sel"][lo:hi], c["gains"][lo:hi])
+        f = bf16_bits_to_f32
+        ref = od.reference_dense(c["h"].float().numpy()[lo:hi], c["sel"].numpy()[lo:hi], c["gains"].numpy()[lo:hi],
+                                 w, f(u16(c["s"])), f(u16(c["b"])), c["sw"].numpy().view(np.uint32), f(u16(c["ss"])),
+                                 f(u16(c["sb"])), F=F, FS=FS, topk=TOPK)
+        err = float(np.abs(y.numpy() - ref).max() / max(np.abs(ref).max(), 1e-30)) if hi > lo else 0.0
+        q.put((rank, err, tuple(y.shape)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("tokens_per_rank", [(7, 5), (12, 0)])
+def test_ep_dispatch_combine_gloo(tokens_per_rank):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, tokens_per_rank, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, shape in res:
+        assert shape == (tokens_per_rank[rank], D)
+        assert err < 1e-5, (rank, err)
