@@ -153,7 +153,7 @@ int hsd_sparse_down_prefill(const void* h, int h_dtype, const float* gains, cons
 /* The causal-conv half of hsd/mamba.py:28-32 (mamba_verify): window = [conv_state; conv_in]
  * (K-1+L rows, conv_state NULL = zeros) is copied to `padded` (conv_in's dtype) and
  * out[t, c] = silu(bias[c] + sum_j w[c, j] * window[t + j, c]) in fp32. conv_in rows are
- * in_stride elements apart (a slice of the in_proj output). 1 <= L <= 64, K <= 8.
+ * in_stride elements apart (a slice of the in_proj output). L >= 1, K == 4.
  * in_dtype f32 / bf16, w_dtype f32 / bf16, out_dtype f32 / f16 / bf16. */
 int hsd_mamba_conv_verify(const void* conv_in, int in_dtype, int64_t in_stride,
                           const void* conv_state, const void* w, int w_dtype, const void* bias,
@@ -165,12 +165,13 @@ int hsd_mamba_conv_verify(const void* conv_in, int in_dtype, int64_t in_stride,
  *   state0 [H, P, N] f32 (NULL = zeros) -> y [L, H*P] (y_dtype f32 / bf16) and
  *   states [L, H, P, N] f32: the state after every row (the per-row checkpoints).
  * dt_t = clamp(softplus(dt + dt_bias), dt_min, dt_max). Rows run as single steps would, so
- * states[n-1] equals n single steps bit for bit. N in {32, 64, 128, 256}, H % G == 0. */
+ * states[n-1] equals n single steps bit for bit. last_only != 0 (a prefill chunk, never rolled
+ * back): only the final state, in states[0] ([1, H, P, N]). N in {32, 64, 128, 256}, H % G == 0. */
 int hsd_mamba_ssm_verify(const void* xbc, int x_dtype, int64_t xbc_stride, const void* dt,
                          int dt_dtype, int64_t dt_stride, const float* A_log, const float* D,
                          const float* dt_bias, float dt_min, float dt_max, const float* state0,
                          float* states, void* y, int y_dtype, int L, int H, int P, int G, int N,
-                         void* stream);
+                         int last_only, void* stream);
 
 /* hsd/mamba.py:47 mamba_rollback(records, n_keep), on device and without recomputation:
  * state_out = states[n_keep-1], conv_out = padded[n_keep : n_keep+K-1] (elem_bytes per

@@ -3,15 +3,17 @@
 // mlx-lm's ssm_update over the kept rows; here every row's state is written once during the
 // verify, so a rollback is a selection and never a recomputation).
 //
-// conv_verify  one thread per channel: the window [conv_state; conv_in] (K-1+L rows) is
-//              copied to `padded` and out[t] = silu(bias + sum_j w[c, j] * padded[t + j]) in
-//              fp32. After keeping n rows the conv state is padded[n : n+K-1].
+// conv_verify  one thread per channel with a rolling 4-row register window: the window
+//              [conv_state; conv_in] (K-1+L rows) is copied to `padded` and out[t] =
+//              silu(bias + sum_j w[c, j] * padded[t + j]) in fp32. After keeping n rows the
+//              conv state is padded[n : n+K-1].
 // ssm_verify   one warp per (head h, channel p); lane l holds state[h, p, l*NPL .. +NPL) in
 //              registers. Rows one after another, exactly as single steps would run them:
 //                dt_t = clamp(softplus(dt[t,h] + dt_bias[h]), dt_min, dt_max)
 //                state = state * exp(dt_t * A_h) + (dt_t * x[t,h,p]) * B[t, g(h), :]
 //                y[t,h,p] = sum_n state * C[t, g(h), :] + D_h * x[t,h,p]   (warp reduction)
-//              and after every row the warp stores its state slice to states[t] (coalesced).
+//              and after every row the warp stores its state slice to states[t] (coalesced);
+//              with last_only (prefill, no rollback) only the final state, to states[0].
 //              A verify of L rows and L single steps run the same instructions per row, so
 //              the state after row n of a verify is bit-identical to n single steps.
 #include "hsd_common.cuh"
@@ -30,22 +32,28 @@ template <typename TI, typename TW, typename TO>
 __global__ void __launch_bounds__(256) conv_verify_kernel(const void* conv_in, int64_t in_stride,
                                                           const void* conv_state, const void* w,
                                                           const void* bias, void* out, void* padded, int L,
-                                                          int C, int K) {
+                                                          int C) {
+  constexpr int K = 4;                             // the model's conv kernel (checked on the host)
   const int c = blockIdx.x * 256 + threadIdx.x;
   if (c >= C) return;
-  float win[8 + 64];                               // K-1 + L <= 71 (checked on the host)
-  const int NW = K - 1 + L;
-  for (int j = 0; j < K - 1; ++j) win[j] = conv_state ? ld<TI>(conv_state, static_cast<int64_t>(j) * C + c) : 0.f;
-  for (int t = 0; t < L; ++t) win[K - 1 + t] = ld<TI>(conv_in, static_cast<int64_t>(t) * in_stride + c);
-  for (int j = 0; j < NW; ++j)
+  float win[K];                                    // rolling window: rows t .. t+K-1 of padded
+  for (int j = 0; j < K - 1; ++j) {
+    win[j] = conv_state ? ld<TI>(conv_state, static_cast<int64_t>(j) * C + c) : 0.f;
     reinterpret_cast<TI*>(padded)[static_cast<int64_t>(j) * C + c] = hsd::from_f32<TI>(win[j]);
+  }
   const float b = bias ? ld<TW>(bias, c) : 0.f;
-  float wk[8];
+  float wk[K];
+#pragma unroll
   for (int j = 0; j < K; ++j) wk[j] = ld<TW>(w, static_cast<int64_t>(c) * K + j);
   for (int t = 0; t < L; ++t) {
+    win[K - 1] = ld<TI>(conv_in, static_cast<int64_t>(t) * in_stride + c);
+    reinterpret_cast<TI*>(padded)[static_cast<int64_t>(K - 1 + t) * C + c] = hsd::from_f32<TI>(win[K - 1]);
     float a = b;
-    for (int j = 0; j < K; ++j) a = fmaf(wk[j], win[t + j], a);
+#pragma unroll
+    for (int j = 0; j < K; ++j) a = fmaf(wk[j], win[j], a);
     reinterpret_cast<TO*>(out)[static_cast<int64_t>(t) * C + c] = hsd::from_f32<TO>(silu_f(a));
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
   }
 }
 
@@ -56,7 +64,7 @@ __global__ void __launch_bounds__(256) ssm_verify_kernel(const void* xbc, int64_
                                                          const float* __restrict__ dt_bias, float dt_min,
                                                          float dt_max, const float* __restrict__ state0,
                                                          float* __restrict__ states, void* y, int L, int H, int P,
-                                                         int G, int N) {
+                                                         int G, int N, int last_only) {
   const int warp_g = (blockIdx.x * 256 + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp_g >= H * P) return;
@@ -88,7 +96,8 @@ __global__ void __launch_bounds__(256) ssm_verify_kernel(const void* xbc, int64_
     if (lane == 0)
       reinterpret_cast<TY*>(y)[static_cast<int64_t>(t) * I + static_cast<int64_t>(h) * P + p] =
           hsd::from_f32<TY>(fmaf(Dh, x, acc));
-    float* dst = states + static_cast<int64_t>(t) * H * P * N + sbase;
+    if (last_only && t != L - 1) continue;         // prefill: the final state only, in states[0]
+    float* dst = states + static_cast<int64_t>(last_only ? 0 : t) * H * P * N + sbase;
     if constexpr (NPL % 4 == 0) {
 #pragma unroll
       for (int i = 0; i < NPL; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(st[i], st[i + 1], st[i + 2], st[i + 3]);
@@ -104,9 +113,9 @@ int conv_dispatch_out(int out_dtype, dim3 grid, cudaStream_t st, const void* con
                       const void* conv_state, const void* w, const void* bias, void* out, void* padded, int L, int C,
                       int K) {
   switch (out_dtype) {
-    case HSD_F32: conv_verify_kernel<TI, TW, float><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K); break;
-    case HSD_F16: conv_verify_kernel<TI, TW, __half><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K); break;
-    case HSD_BF16: conv_verify_kernel<TI, TW, __nv_bfloat16><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K); break;
+    case HSD_F32: conv_verify_kernel<TI, TW, float><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C); break;
+    case HSD_F16: conv_verify_kernel<TI, TW, __half><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C); break;
+    case HSD_BF16: conv_verify_kernel<TI, TW, __nv_bfloat16><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C); break;
     default: return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_conv_verify: out_dtype %d", out_dtype);
   }
   return hsd::check_launch("hsd_mamba_conv_verify");
@@ -126,12 +135,13 @@ int conv_dispatch_w(int w_dtype, int out_dtype, dim3 grid, cudaStream_t st, cons
 template <typename TX, typename TD, typename TY>
 int ssm_dispatch_n(int N, dim3 grid, cudaStream_t st, const void* xbc, int64_t xbc_stride, const void* dt,
                    int64_t dt_stride, const float* A_log, const float* Dp, const float* dt_bias, float dt_min,
-                   float dt_max, const float* state0, float* states, void* y, int L, int H, int P, int G) {
+                   float dt_max, const float* state0, float* states, void* y, int L, int H, int P, int G,
+                   int last_only) {
   switch (N) {
-    case 32: ssm_verify_kernel<TX, TD, TY, 1><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N); break;
-    case 64: ssm_verify_kernel<TX, TD, TY, 2><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N); break;
-    case 128: ssm_verify_kernel<TX, TD, TY, 4><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N); break;
-    case 256: ssm_verify_kernel<TX, TD, TY, 8><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N); break;
+    case 32: ssm_verify_kernel<TX, TD, TY, 1><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only); break;
+    case 64: ssm_verify_kernel<TX, TD, TY, 2><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only); break;
+    case 128: ssm_verify_kernel<TX, TD, TY, 4><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only); break;
+    case 256: ssm_verify_kernel<TX, TD, TY, 8><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only); break;
     default: return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_ssm_verify: N must be 32, 64, 128 or 256 (got %d)", N);
   }
   return hsd::check_launch("hsd_mamba_ssm_verify");
@@ -141,11 +151,11 @@ template <typename TX>
 int ssm_dispatch(int dt_dtype, int y_dtype, int N, dim3 grid, cudaStream_t st, const void* xbc, int64_t xbc_stride,
                  const void* dt, int64_t dt_stride, const float* A_log, const float* Dp, const float* dt_bias,
                  float dt_min, float dt_max, const float* state0, float* states, void* y, int L, int H, int P,
-                 int G) {
+                 int G, int last_only) {
 #define HSD_SSM_Y(TD)                                                                                            \
   switch (y_dtype) {                                                                                           \
-    case HSD_F32: return ssm_dispatch_n<TX, TD, float>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G); \
-    case HSD_BF16: return ssm_dispatch_n<TX, TD, __nv_bfloat16>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G); \
+    case HSD_F32: return ssm_dispatch_n<TX, TD, float>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only); \
+    case HSD_BF16: return ssm_dispatch_n<TX, TD, __nv_bfloat16>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only); \
   }                                                                                                            \
   return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_ssm_verify: y_dtype %d (f32 or bf16)", y_dtype);
   switch (dt_dtype) {
@@ -162,8 +172,8 @@ extern "C" int hsd_mamba_conv_verify(const void* conv_in, int in_dtype, int64_t 
                                      const void* w, int w_dtype, const void* bias, void* out, int out_dtype,
                                      void* padded, int L, int C, int K, void* stream) {
   if (!conv_in || !w || !out || !padded) return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_conv_verify: null pointer");
-  if (L < 1 || L > 64 || C < 1 || K < 1 || K > 8 || in_stride < C)
-    return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_conv_verify: need 1 <= L <= 64, 1 <= K <= 8, in_stride >= C");
+  if (L < 1 || C < 1 || K != 4 || in_stride < C)
+    return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_conv_verify: need L >= 1, K == 4, in_stride >= C");
   dim3 grid((C + 255) / 256);
   cudaStream_t st = hsd::as_stream(stream);
   switch (in_dtype) {
@@ -176,7 +186,7 @@ extern "C" int hsd_mamba_conv_verify(const void* conv_in, int in_dtype, int64_t 
 extern "C" int hsd_mamba_ssm_verify(const void* xbc, int x_dtype, int64_t xbc_stride, const void* dt, int dt_dtype,
                                     int64_t dt_stride, const float* A_log, const float* D, const float* dt_bias,
                                     float dt_min, float dt_max, const float* state0, float* states, void* y,
-                                    int y_dtype, int L, int H, int P, int G, int N, void* stream) {
+                                    int y_dtype, int L, int H, int P, int G, int N, int last_only, void* stream) {
   if (!xbc || !dt || !A_log || !D || !dt_bias || !states || !y)
     return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_ssm_verify: null pointer");
   if (L < 1 || H < 1 || P < 1 || G < 1 || H % G != 0 || xbc_stride < static_cast<int64_t>(H) * P + 2 * G * N)
@@ -187,8 +197,8 @@ extern "C" int hsd_mamba_ssm_verify(const void* xbc, int x_dtype, int64_t xbc_st
   dim3 grid(static_cast<unsigned>((warps * 32 + 255) / 256));
   cudaStream_t st = hsd::as_stream(stream);
   switch (x_dtype) {
-    case HSD_F32: return ssm_dispatch<float>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G);
-    case HSD_BF16: return ssm_dispatch<__nv_bfloat16>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G);
+    case HSD_F32: return ssm_dispatch<float>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only);
+    case HSD_BF16: return ssm_dispatch<__nv_bfloat16>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only);
   }
   return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_ssm_verify: x_dtype %d (f32 or bf16)", x_dtype);
 }

@@ -109,27 +109,29 @@ def conv_verify(conv_in, conv_state, conv_w, conv_b, out_dtype=torch.bfloat16):
 
 
 def ssm_verify(xbc, dt, A_log, D, dt_bias, state0, *, H, P, G, N, time_step_limit=(0.0, float("inf")),
-               y_dtype=torch.float32):
-    """xbc [L, >= H*P + 2GN] (x | B | C), dt [L, >= H] -> (y [L, H*P], states [L, H, P, N] fp32)."""
+               y_dtype=torch.float32, checkpoints=True):
+    """xbc [L, >= H*P + 2GN] (x | B | C), dt [L, >= H] -> (y [L, H*P], states [L, H, P, N] fp32:
+    the state after every row; with checkpoints=False only the final one, [1, H, P, N])."""
     L = xbc.shape[0]
     if xbc.stride(1) != 1 or dt.stride(1) != 1:
         raise ValueError("ssm_verify: rows must be contiguous")
     if state0 is not None and (state0.dtype != torch.float32 or not state0.is_contiguous()):
         state0 = state0.float().contiguous()
     y = torch.empty((L, H * P), dtype=y_dtype, device=xbc.device)
-    states = torch.empty((L, H, P, N), dtype=torch.float32, device=xbc.device)
+    states = torch.empty((L if checkpoints else 1, H, P, N), dtype=torch.float32, device=xbc.device)
     lo, hi = time_step_limit
     _lib.call("hsd_mamba_ssm_verify", _lib.ptr(xbc), _lib.dtype_code(xbc, "xbc"), xbc.stride(0), _lib.ptr(dt),
               _lib.dtype_code(dt, "dt"), dt.stride(0), _lib.ptr(A_log), _lib.ptr(D), _lib.ptr(dt_bias), float(lo),
               float(hi), _lib.ptr(state0), _lib.ptr(states), _lib.ptr(y), _lib.dtype_code(y, "y"), L, H, P, G, N,
-              _lib.stream_of(xbc))
+              0 if checkpoints else 1, _lib.stream_of(xbc))
     return y, states
 
 
-def mamba_verify(block, x3, cache, records):
+def mamba_verify(block, x3, cache, records, checkpoints=True):
     """hsd/mamba.py:19 -- one Mamba-2 block on x3 [1, L, D] with the cache advanced by L rows;
     `records` gets what a later rollback needs (the padded conv window and the per-row states).
-    Returns x3 + mixer(norm(x3))."""
+    checkpoints=False (a prompt chunk, never rolled back) keeps the final state only and records
+    nothing. Returns x3 + mixer(norm(x3))."""
     b = block
     x = x3[0]
     L = x.shape[0]
@@ -138,10 +140,11 @@ def mamba_verify(block, x3, cache, records):
     proj = h @ b.in_proj.t()                                      # [L, I + conv_dim + H]
     co, padded = conv_verify(proj[:, I:I + Cd], cache[0], b.conv_w, b.conv_b)
     y, states = ssm_verify(co, proj[:, I + Cd:], b.A_log, b.D, b.dt_bias, cache[1], H=b.H, P=b.P, G=b.G, N=b.N,
-                           time_step_limit=b.time_step_limit)
+                           time_step_limit=b.time_step_limit, checkpoints=checkpoints)
     cache[0] = padded[L:]                                         # the last K-1 rows of the window
-    cache[1] = states[L - 1]
-    records.append((cache, padded, states, b.K))
+    cache[1] = states[-1]
+    if checkpoints:
+        records.append((cache, padded, states, b.K))
     yn = gated_rms_norm(y, proj[:, :I], b.gate_norm_w, I // b.G, b.eps, x.dtype)
     return x3 + (yn @ b.out_proj.t())[None]
 

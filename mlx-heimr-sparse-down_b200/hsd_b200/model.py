@@ -181,7 +181,8 @@ class MoEBlock:
         sel, gains, hcat = self.front(x)
         a = self.a
         if mode == "dense":
-            return x + self.down_dense(hcat, sel, gains).to(x.dtype)
+            # the residual added in fp32 and rounded once, as the kernels do
+            return (x.float() + self.down_dense(hcat, sel, gains)).to(x.dtype)
         return sparse_down(hcat, sel, gains, self.pw, self.ps, self.pb, self.spw, self.sps, self.spb, F=a.F,
                            FS=a.FS, D=a.hidden, topk=a.topk, resid=x)
 
@@ -295,7 +296,12 @@ class NemotronModel:
         return self.embeddings[ids]
 
     def head_fn(self, h):
-        return (h @ self.lm_head.t()).float()
+        """Logits in fp32 (bf16 operands, fp32 output): bf16 logits near 4 are 1/32 apart, which
+        turns many greedy choices into exact ties."""
+        if h.is_cuda:
+            return torch.mm(h.reshape(-1, h.shape[-1]), self.lm_head.t(), out_dtype=torch.float32).view(
+                *h.shape[:-1], -1)
+        return h.float() @ self.lm_head.float().t()
 
     def logits(self, x):
         return self.head_fn(rms_norm(x, self.norm_f, self.args.eps))
@@ -313,7 +319,7 @@ class NemotronModel:
             elif t == "attention":
                 x = blk(x, cache[l])
             else:
-                x = hm.mamba_verify(blk.blk, x[None], cache[l], records)[0]
+                x = hm.mamba_verify(blk.blk, x[None], cache[l], records, checkpoints=multi != "prefill")[0]
         return x
 
     def prefill(self, tokens, cache, chunk=512, on_hidden=None):
@@ -348,26 +354,42 @@ class NemotronModel:
         hm.mamba_rollback(self._records, n_keep)
 
     # ---- generation (greedy)
-    def generate(self, prompt, max_tokens=128, chunk=512):
-        """Greedy decoding (hsd/model.py:291) -> (tokens, stats)."""
+    def _pick(self, x):
+        """Greedy choice for the last row of x: (token, top-1 minus top-2 logit), one host read."""
+        top = torch.topk(self.logits(x[-1:]), 2, dim=-1)
+        v, i = top.values[0], top.indices[0]
+        tok, margin = torch.stack([i[0].float(), v[0] - v[1]]).tolist()
+        return int(tok), margin
+
+    def generate(self, prompt, max_tokens=128, chunk=512, forced=None):
+        """Greedy decoding (hsd/model.py:291) -> (tokens, stats). stats["margins"] holds the
+        top-1 minus top-2 logit of every choice. With `forced` (a token list) the loop feeds
+        forced[i] instead of its own choice (teacher forcing) and still returns its choices."""
         prompt = torch.as_tensor(prompt, dtype=torch.long, device=self.device)
         cache = self.make_cache()
         torch.cuda.synchronize(self.device)
         t0 = time.perf_counter()
         h = self.prefill(prompt, cache, chunk)
-        tok = int(torch.argmax(self.logits(h), -1).item())
+        tok, mg = self._pick(h)
         t1 = time.perf_counter()
-        out = [tok]
+        out, margins = [tok], [mg]
         while len(out) < max_tokens:
-            x = self.step(self.embed(torch.tensor([tok], device=self.device)), cache)
-            tok = int(torch.argmax(self.logits(x), -1).item())
+            feed = forced[len(out) - 1] if forced is not None else tok
+            x = self.step(self.embed(torch.tensor([feed], device=self.device)), cache)
+            tok, mg = self._pick(x)
             out.append(tok)
+            margins.append(mg)
         t2 = time.perf_counter()
         return out, dict(mode=self.mode, prompt_tokens=int(prompt.shape[0]), prompt_s=t1 - t0, gen_tokens=len(out),
-                         decode_s=t2 - t1, decode_tps=(len(out) - 1) / max(t2 - t1, 1e-9))
+                         decode_s=t2 - t1, decode_tps=(len(out) - 1) / max(t2 - t1, 1e-9), margins=margins)
 
-    def generate_mtp(self, prompt, mtp, n_draft=2, max_tokens=128, chunk=512):
-        """Greedy speculative decoding with the MTP head (hsd/model.py:366-443) -> (tokens, stats)."""
+    def generate_mtp(self, prompt, mtp, n_draft=2, max_tokens=128, chunk=512, replay=None):
+        """Greedy speculative decoding with the MTP head (hsd/model.py:366-443) -> (tokens, stats).
+
+        replay (a token list, e.g. an earlier greedy run's output) replaces the head's drafts
+        with the tokens that follow in that list -- forced acceptance, which times the verify
+        and rollback at acceptances a = 0..k that a random-init head never reaches. The accept
+        rule is unchanged, so the output is still this model's own greedy sequence."""
         prompt = torch.as_tensor(prompt, dtype=torch.long, device=self.device)
         cache = self.make_cache()
         mtp.reset()
@@ -375,7 +397,7 @@ class NemotronModel:
 
         def on_hidden(i, x):                       # the head's prefill: rows (h_p, tok_{p+1})
             nxt = prompt[i + 1:i + 1 + x.shape[0]]
-            if nxt.shape[0] > 0:
+            if nxt.shape[0] > 0 and replay is None:
                 mtp(x[:nxt.shape[0]], nxt)
             last_h.append(x[-1:])
 
@@ -389,13 +411,17 @@ class NemotronModel:
         steps, acc = 0, []
         bs = n_draft + 1
         while len(out) < max_tokens:
-            d, hd = mtp(torch.cat(pend_h, 0), torch.tensor(pend_t, device=self.device))
-            drafts = [d[-1:]]
-            hd = hd[-1:]
-            for _ in range(1, n_draft):            # chain the head on its own hidden output
-                d, hd = mtp(hd, drafts[-1])
-                drafts.append(d)
-            draft = torch.cat(drafts)
+            if replay is None:
+                d, hd = mtp(torch.cat(pend_h, 0), torch.tensor(pend_t, device=self.device))
+                drafts = [d[-1:]]
+                hd = hd[-1:]
+                for _ in range(1, n_draft):        # chain the head on its own hidden output
+                    d, hd = mtp(hd, drafts[-1])
+                    drafts.append(d)
+                draft = torch.cat(drafts)
+            else:
+                nxt = replay[len(out):len(out) + n_draft]
+                draft = torch.tensor(nxt + [0] * (n_draft - len(nxt)), device=self.device)
             ids = torch.cat([torch.tensor([tok], device=self.device), draft])
             x = self.verify_step(self.embed(ids), cache)
             tgt = torch.argmax(self.logits(x), -1)
@@ -403,7 +429,7 @@ class NemotronModel:
             a = next((i for i in range(bs - 1) if dl[i] != tl[i]), bs - 1)
             new = (dl[:a] + [tl[a]])[:max_tokens - len(out)]
             self.rollback(cache, a + 1, bs)
-            if n_draft > 1:
+            if n_draft > 1 and replay is None:
                 mtp.trim(n_draft - 1)              # drop the chained speculative rows
             pend_h = [x[i:i + 1] for i in range(len(new))]
             pend_t = list(new)
@@ -414,7 +440,18 @@ class NemotronModel:
         t2 = time.perf_counter()
         return out, dict(mode=self.mode, n_draft=n_draft, steps=steps, accepted_mean=sum(acc) / max(1, len(acc)),
                          accepted_hist=[acc.count(k) for k in range(n_draft + 1)], gen_tokens=len(out),
-                         prompt_s=t1 - t0, decode_s=t2 - t1, decode_tps=(len(out) - 1) / max(t2 - t1, 1e-9))
+                         prompt_s=t1 - t0, decode_s=t2 - t1, decode_tps=(len(out) - 1) / max(t2 - t1, 1e-9),
+                         replay=replay is not None)
+
+
+def identical_prefix(a, b):
+    """Length of the common prefix of two token lists."""
+    n = 0
+    for x, y in zip(a, b):
+        if x != y:
+            break
+        n += 1
+    return n
 
 
 class MTPHead:

@@ -113,3 +113,19 @@ def test_block_vs_oracle_mixer(cuda):
     hn = om.rms_norm(f32_np(x[0]), f32_np(blk.norm_w), blk.eps)
     ref, _, _ = om.mixer_rows(p, hn, None, None)
     assert rel_err(f32_np(out[0] - x[0]), ref) < 3e-2              # bf16 matmuls and activations
+
+
+@pytest.mark.gpu
+def test_long_chunk_final_state_only(cuda):
+    """A prompt chunk of 300 rows (no rollback): the final state alone equals the last
+    checkpoint of the full run, and the conv window is the chunk's last rows."""
+    L = 300
+    xbc, dt, A_log, D, dt_bias, state0 = _inputs(L, 31, cuda)
+    y1, s_all = hm.ssm_verify(xbc, dt, A_log, D, dt_bias, state0, H=H, P=P, G=G, N=N)
+    y2, s_last = hm.ssm_verify(xbc, dt, A_log, D, dt_bias, state0, H=H, P=P, G=G, N=N, checkpoints=False)
+    assert s_last.shape[0] == 1 and torch.equal(s_last[0], s_all[-1]) and torch.equal(y1, y2)
+    conv_in = torch.randn((L, 512), device=cuda).to(torch.bfloat16)
+    w = torch.randn((512, K), device=cuda)
+    out, padded = hm.conv_verify(conv_in, None, w, None, out_dtype=torch.float32)
+    oout, opad = om.conv_rows(f32_np(conv_in), None, f32_np(w), None)
+    assert np.array_equal(f32_np(padded), opad) and rel_err(f32_np(out), oout) < 1e-5
