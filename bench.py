@@ -216,9 +216,10 @@ def max_over_ranks(v, dist_on, device):
     return float(t.item())
 
 
-def timed(fn, steps, warmup, device, dist_on):
+def timed(fn, steps, warmup, device, dist_on, label="hsd_timed"):
     """Device time (ms) of `steps` calls of fn(i) after `warmup` calls, CUDA events on the
-    current stream, barrier + synchronize on both sides, max over ranks."""
+    current stream, barrier + synchronize on both sides, max over ranks. The timed calls sit
+    in an NVTX range named `label` (ncu --nvtx --nvtx-include "<label>/" lists its launches)."""
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize(device)
@@ -227,10 +228,12 @@ def timed(fn, steps, warmup, device, dist_on):
     st = torch.cuda.current_stream(device)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push(label)
     e0.record(st)
     for i in range(steps):
         fn(warmup + i)
     e1.record(st)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(device)
     barrier(dist_on)
     return max_over_ranks(e0.elapsed_time(e1), dist_on, device)

@@ -180,6 +180,68 @@ int hsd_mamba_rollback(const float* states, const void* padded, int elem_bytes, 
                        int H, int P, int N, int C, int K, float* state_out, void* conv_out,
                        void* stream);
 
+/* Resident-buffer forms of the two verify kernels, for decode loops replayed from a CUDA
+ * graph (no counterpart in the reference, whose rollback re-runs ssm_update over the kept
+ * rows, hsd/mamba.py:47-56). The previous call's outputs are the inputs: the conv window is
+ * padded[*n_keep .. *n_keep+K-2] and the SSM state states[*n_keep-1], where *n_keep (device
+ * memory, 1 <= *n_keep <= rows) is the number of rows the previous call kept -- 1 after a
+ * plain step, a+1 after a verify whose first a drafts were accepted. The call writes the
+ * window and its L new rows to padded[0 .. K-2+L] and the state after each row to
+ * states[0 .. L-1], in place. padded [rows + K - 1, C] (zeros before the first call),
+ * states [rows, H, P, N] fp32 (zeros before the first call), 1 <= L <= rows. A *n_keep
+ * outside 1..rows is read as 1 and recorded as HSD_ERR_INDEX in the status word. */
+int hsd_mamba_conv_step(const void* conv_in, int in_dtype, int64_t in_stride, void* padded,
+                        const int* n_keep, int rows, const void* w, int w_dtype, const void* bias,
+                        void* out, int out_dtype, int L, int C, int K, void* stream);
+
+int hsd_mamba_ssm_step(const void* xbc, int x_dtype, int64_t xbc_stride, const void* dt,
+                       int dt_dtype, int64_t dt_stride, const float* A_log, const float* D,
+                       const float* dt_bias, float dt_min, float dt_max, float* states,
+                       const int* n_keep, int rows, void* y, int y_dtype, int L, int H, int P,
+                       int G, int N, void* stream);
+
+/* ---- MoE front end (the caller of the down kernel) -------------------------------- */
+
+/* hsd/model.py:110-121 front(): the routed up projections (mlx gather_qmm of fc1 over the
+ * selected experts) and the shared expert's up_proj, each followed by relu2, fused into one
+ * launch that writes the down kernel's input directly:
+ *   h[b, k*F + f]    = relu(sum_d Wu[sel[b,k]][f, d] * x[b, d])^2   for k < topk, f < F
+ *   h[b, topk*F + f] = relu(sum_d Wsu[f, d] * x[b, d])^2             for f < FS
+ * Up weights in the checkpoint layout along the hidden axis: uw [E, F, D/8] u32, us / ub
+ * [E, F, D/64] (s_dtype); suw [FS, D/8], sus / sub [FS, D/64]. x [B, D] with row stride
+ * x_stride elements; h [B, topk*F + FS] contiguous. fp32 accumulation, one rounding to
+ * h_dtype. D % 64 == 0, D <= 8192, uw / suw 16-byte aligned; topk == 0 (shared only) and
+ * FS == 0 (routed only) are allowed. An expert id outside [0, E) gives zeros for that slot
+ * and HSD_ERR_INDEX in the status word. */
+int hsd_moe_up_decode(const void* x, int x_dtype, int64_t x_stride, const int32_t* sel,
+                      const uint32_t* uw, const void* us, const void* ub, int s_dtype,
+                      const uint32_t* suw, const void* sus, const void* sub, void* h,
+                      int h_dtype, int B, int D, int F, int FS, int topk, int E, void* stream);
+
+/* hsd/model.py:132-133 decode_dense (the stock path: mlx gather_qmm of fc2 over the
+ * selected experts and the shared expert's down_proj), as the sparse kernel's comparison
+ * point on the same device: every weight of the selected experts is read from the checkpoint
+ * layout (w [E, D, F/8], s / b [E, D, F/64]; sw [D, FS/8], ss / sb [D, FS/64]), fp32
+ * accumulation, the part's gain applied, the partial rows written to part [B, topk+1, D]
+ * fp32 (caller-owned workspace) and summed in slot order (+ resid) into y [B, D]. Same
+ * h / sel / gains / resid / y conventions as hsd_sparse_down_decode. D % 32 == 0, F and FS
+ * multiples of 64 and <= 8192, w / sw 16-byte aligned. */
+int hsd_dense_down_decode(const void* h, int h_dtype, const int32_t* sel, const float* gains,
+                          const uint32_t* w, const void* s, const void* b, int s_dtype,
+                          const uint32_t* sw, const void* ss, const void* sb, const void* resid,
+                          void* y, int y_dtype, float* part, int B, int D, int F, int FS, int topk,
+                          int E, void* stream);
+
+/* The model's other 4-bit linears at decode (mlx QuantizedLinear, the layers around the hot
+ * path: Mamba in / out projections, attention projections, lm_head), same kernel:
+ *   y[b, o] = (resid[b, o] +) sum_i W[o, i] * x[b, i]
+ * w [out_f, in_f/8] u32, s / b [out_f, in_f/64] (s_dtype); x [B, in_f] with row stride
+ * x_stride; resid (may be NULL) and y [B, out_f] contiguous in y_dtype. fp32 accumulation,
+ * the residual added in fp32, one rounding. in_f % 64 == 0, in_f <= 8192, w 16-byte aligned. */
+int hsd_qlinear_decode(const void* x, int x_dtype, int64_t x_stride, const uint32_t* w, const void* s,
+                       const void* b, int s_dtype, const void* resid, void* y, int y_dtype, int B,
+                       int in_f, int out_f, void* stream);
+
 /* ---- allocation-free prefill ------------------------------------------------------ */
 
 /* No counterpart in the reference. For callers that cannot call cudaMalloc (code running

@@ -23,6 +23,8 @@ int set_error(int code, const char* fmt, ...) {
 int hsd_read_status_decode(int* out, cudaStream_t st);
 int hsd_read_status_prefill(int* out, cudaStream_t st);
 int hsd_read_status_gemm(int* out, cudaStream_t st);
+int hsd_read_status_up(int* out, cudaStream_t st);
+int hsd_read_status_mamba(int* out, cudaStream_t st);
 
 extern "C" const char* hsd_last_error_string(void) { return hsd::g_last_error; }
 
@@ -33,7 +35,8 @@ extern "C" int hsd_device_status(int* status_out, void* stream) {
   cudaStream_t st = hsd::as_stream(stream);
   int first = HSD_OK;
   int (*readers[])(int*, cudaStream_t) = {hsd_read_status_decode, hsd_read_status_prefill,
-                                                hsd_read_status_gemm};
+                                                hsd_read_status_gemm, hsd_read_status_up,
+                                                hsd_read_status_mamba};
   for (auto rd : readers) {
     int v = HSD_OK;
     int rc = rd(&v, st);

@@ -16,9 +16,30 @@
 //              with last_only (prefill, no rollback) only the final state, to states[0].
 //              A verify of L rows and L single steps run the same instructions per row, so
 //              the state after row n of a verify is bit-identical to n single steps.
+//
+// The *_step entry points are the same kernels on resident buffers, for decode loops that
+// replay a captured CUDA graph: the conv window and the SSM state are read from the previous
+// call's own output rows, selected by a device-side accepted-row count n_keep (the window
+// padded[n_keep .. n_keep+K-2], the state states[n_keep-1]), and the new rows are written
+// over the same buffers. Each thread (conv) or lane (ssm) reads its whole slice before it
+// writes any of it, and only its own slice, so the in-place update needs no barrier. A
+// rollback is then one integer written on the device.
 #include "hsd_common.cuh"
 
+HSD_DEFINE_STATUS(mamba)
+
 namespace {
+
+// The accepted-row count of a resident-buffer call: *n_keep, or 1 (with HSD_ERR_INDEX in the
+// status word) when it lies outside 1..rows.
+__device__ __forceinline__ int read_keep(const int* n_keep, int rows) {
+  const int k = *n_keep;
+  if (k < 1 || k > rows) {
+    if (threadIdx.x == 0) atomicCAS(&hsd_status_word_mamba, 0, HSD_ERR_INDEX);
+    return 1;
+  }
+  return k;
+}
 
 template <typename T>
 __device__ __forceinline__ float ld(const void* p, int64_t i) {
@@ -32,15 +53,18 @@ template <typename TI, typename TW, typename TO>
 __global__ void __launch_bounds__(256) conv_verify_kernel(const void* conv_in, int64_t in_stride,
                                                           const void* conv_state, const void* w,
                                                           const void* bias, void* out, void* padded, int L,
-                                                          int C) {
+                                                          int C, const int* n_keep, int rows) {
   constexpr int K = 4;                             // the model's conv kernel (checked on the host)
   const int c = blockIdx.x * 256 + threadIdx.x;
   if (c >= C) return;
+  if (n_keep)                                      // resident form: the window is padded[n_keep ..]
+    conv_state = static_cast<const TI*>(padded) + static_cast<int64_t>(read_keep(n_keep, rows)) * C;
   float win[K];                                    // rolling window: rows t .. t+K-1 of padded
-  for (int j = 0; j < K - 1; ++j) {
-    win[j] = conv_state ? ld<TI>(conv_state, static_cast<int64_t>(j) * C + c) : 0.f;
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) win[j] = conv_state ? ld<TI>(conv_state, static_cast<int64_t>(j) * C + c) : 0.f;
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j)
     reinterpret_cast<TI*>(padded)[static_cast<int64_t>(j) * C + c] = hsd::from_f32<TI>(win[j]);
-  }
   const float b = bias ? ld<TW>(bias, c) : 0.f;
   float wk[K];
 #pragma unroll
@@ -62,9 +86,9 @@ __global__ void __launch_bounds__(256) ssm_verify_kernel(const void* xbc, int64_
                                                          int64_t dt_stride, const float* __restrict__ A_log,
                                                          const float* __restrict__ Dp,
                                                          const float* __restrict__ dt_bias, float dt_min,
-                                                         float dt_max, const float* __restrict__ state0,
-                                                         float* __restrict__ states, void* y, int L, int H, int P,
-                                                         int G, int N, int last_only) {
+                                                         float dt_max, const float* state0, float* states,
+                                                         void* y, int L, int H, int P, int G, int N, int last_only,
+                                                         const int* n_keep, int rows) {
   const int warp_g = (blockIdx.x * 256 + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp_g >= H * P) return;
@@ -72,6 +96,7 @@ __global__ void __launch_bounds__(256) ssm_verify_kernel(const void* xbc, int64_
   const int g = h / (H / G);
   const int I = H * P;
   const int64_t sbase = (static_cast<int64_t>(h) * P + p) * N + lane * NPL;   // this lane's slice
+  if (n_keep) state0 = states + static_cast<int64_t>(read_keep(n_keep, rows) - 1) * H * P * N;
   float st[NPL];
 #pragma unroll
   for (int i = 0; i < NPL; ++i) st[i] = state0 ? state0[sbase + i] : 0.f;
@@ -111,11 +136,11 @@ __global__ void __launch_bounds__(256) ssm_verify_kernel(const void* xbc, int64_
 template <typename TI, typename TW>
 int conv_dispatch_out(int out_dtype, dim3 grid, cudaStream_t st, const void* conv_in, int64_t in_stride,
                       const void* conv_state, const void* w, const void* bias, void* out, void* padded, int L, int C,
-                      int K) {
+                      const int* n_keep, int rows) {
   switch (out_dtype) {
-    case HSD_F32: conv_verify_kernel<TI, TW, float><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C); break;
-    case HSD_F16: conv_verify_kernel<TI, TW, __half><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C); break;
-    case HSD_BF16: conv_verify_kernel<TI, TW, __nv_bfloat16><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C); break;
+    case HSD_F32: conv_verify_kernel<TI, TW, float><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows); break;
+    case HSD_F16: conv_verify_kernel<TI, TW, __half><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows); break;
+    case HSD_BF16: conv_verify_kernel<TI, TW, __nv_bfloat16><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows); break;
     default: return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_conv_verify: out_dtype %d", out_dtype);
   }
   return hsd::check_launch("hsd_mamba_conv_verify");
@@ -124,10 +149,10 @@ int conv_dispatch_out(int out_dtype, dim3 grid, cudaStream_t st, const void* con
 template <typename TI>
 int conv_dispatch_w(int w_dtype, int out_dtype, dim3 grid, cudaStream_t st, const void* conv_in, int64_t in_stride,
                     const void* conv_state, const void* w, const void* bias, void* out, void* padded, int L, int C,
-                    int K) {
+                    const int* n_keep, int rows) {
   switch (w_dtype) {
-    case HSD_F32: return conv_dispatch_out<TI, float>(out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K);
-    case HSD_BF16: return conv_dispatch_out<TI, __nv_bfloat16>(out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K);
+    case HSD_F32: return conv_dispatch_out<TI, float>(out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows);
+    case HSD_BF16: return conv_dispatch_out<TI, __nv_bfloat16>(out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows);
   }
   return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_conv_verify: w_dtype %d (f32 or bf16)", w_dtype);
 }
@@ -136,12 +161,12 @@ template <typename TX, typename TD, typename TY>
 int ssm_dispatch_n(int N, dim3 grid, cudaStream_t st, const void* xbc, int64_t xbc_stride, const void* dt,
                    int64_t dt_stride, const float* A_log, const float* Dp, const float* dt_bias, float dt_min,
                    float dt_max, const float* state0, float* states, void* y, int L, int H, int P, int G,
-                   int last_only) {
+                   int last_only, const int* n_keep, int rows) {
   switch (N) {
-    case 32: ssm_verify_kernel<TX, TD, TY, 1><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only); break;
-    case 64: ssm_verify_kernel<TX, TD, TY, 2><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only); break;
-    case 128: ssm_verify_kernel<TX, TD, TY, 4><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only); break;
-    case 256: ssm_verify_kernel<TX, TD, TY, 8><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only); break;
+    case 32: ssm_verify_kernel<TX, TD, TY, 1><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
+    case 64: ssm_verify_kernel<TX, TD, TY, 2><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
+    case 128: ssm_verify_kernel<TX, TD, TY, 4><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
+    case 256: ssm_verify_kernel<TX, TD, TY, 8><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
     default: return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_ssm_verify: N must be 32, 64, 128 or 256 (got %d)", N);
   }
   return hsd::check_launch("hsd_mamba_ssm_verify");
@@ -151,11 +176,11 @@ template <typename TX>
 int ssm_dispatch(int dt_dtype, int y_dtype, int N, dim3 grid, cudaStream_t st, const void* xbc, int64_t xbc_stride,
                  const void* dt, int64_t dt_stride, const float* A_log, const float* Dp, const float* dt_bias,
                  float dt_min, float dt_max, const float* state0, float* states, void* y, int L, int H, int P,
-                 int G, int last_only) {
+                 int G, int last_only, const int* n_keep, int rows) {
 #define HSD_SSM_Y(TD)                                                                                            \
   switch (y_dtype) {                                                                                           \
-    case HSD_F32: return ssm_dispatch_n<TX, TD, float>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only); \
-    case HSD_BF16: return ssm_dispatch_n<TX, TD, __nv_bfloat16>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only); \
+    case HSD_F32: return ssm_dispatch_n<TX, TD, float>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only, n_keep, rows); \
+    case HSD_BF16: return ssm_dispatch_n<TX, TD, __nv_bfloat16>(N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only, n_keep, rows); \
   }                                                                                                            \
   return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_ssm_verify: y_dtype %d (f32 or bf16)", y_dtype);
   switch (dt_dtype) {
@@ -168,39 +193,77 @@ int ssm_dispatch(int dt_dtype, int y_dtype, int N, dim3 grid, cudaStream_t st, c
 
 }  // namespace
 
-extern "C" int hsd_mamba_conv_verify(const void* conv_in, int in_dtype, int64_t in_stride, const void* conv_state,
-                                     const void* w, int w_dtype, const void* bias, void* out, int out_dtype,
-                                     void* padded, int L, int C, int K, void* stream) {
-  if (!conv_in || !w || !out || !padded) return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_conv_verify: null pointer");
+namespace {
+
+int conv_impl(const char* who, const void* conv_in, int in_dtype, int64_t in_stride, const void* conv_state,
+              const void* w, int w_dtype, const void* bias, void* out, int out_dtype, void* padded, int L, int C,
+              int K, const int* n_keep, int rows, void* stream) {
+  if (!conv_in || !w || !out || !padded) return hsd::set_error(HSD_ERR_ARG, "%s: null pointer", who);
   if (L < 1 || C < 1 || K != 4 || in_stride < C)
-    return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_conv_verify: need L >= 1, K == 4, in_stride >= C");
+    return hsd::set_error(HSD_ERR_SHAPE, "%s: need L >= 1, K == 4, in_stride >= C", who);
   dim3 grid((C + 255) / 256);
   cudaStream_t st = hsd::as_stream(stream);
   switch (in_dtype) {
-    case HSD_F32: return conv_dispatch_w<float>(w_dtype, out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K);
-    case HSD_BF16: return conv_dispatch_w<__nv_bfloat16>(w_dtype, out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, K);
+    case HSD_F32: return conv_dispatch_w<float>(w_dtype, out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows);
+    case HSD_BF16: return conv_dispatch_w<__nv_bfloat16>(w_dtype, out_dtype, grid, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows);
   }
-  return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_conv_verify: in_dtype %d (f32 or bf16)", in_dtype);
+  return hsd::set_error(HSD_ERR_DTYPE, "%s: in_dtype %d (f32 or bf16)", who, in_dtype);
+}
+
+int ssm_impl(const char* who, const void* xbc, int x_dtype, int64_t xbc_stride, const void* dt, int dt_dtype,
+             int64_t dt_stride, const float* A_log, const float* D, const float* dt_bias, float dt_min, float dt_max,
+             const float* state0, float* states, void* y, int y_dtype, int L, int H, int P, int G, int N,
+             int last_only, const int* n_keep, int rows, void* stream) {
+  if (!xbc || !dt || !A_log || !D || !dt_bias || !states || !y)
+    return hsd::set_error(HSD_ERR_ARG, "%s: null pointer", who);
+  if (L < 1 || H < 1 || P < 1 || G < 1 || H % G != 0 || xbc_stride < static_cast<int64_t>(H) * P + 2 * G * N)
+    return hsd::set_error(HSD_ERR_SHAPE, "%s: bad shape (H %% G == 0, xbc_stride >= H*P + 2*G*N)", who);
+  if (!hsd::aligned(states, 16) || (state0 && !hsd::aligned(state0, 16)))
+    return hsd::set_error(HSD_ERR_ALIGN, "%s: states must be 16-byte aligned", who);
+  const int64_t warps = static_cast<int64_t>(H) * P;
+  dim3 grid(static_cast<unsigned>((warps * 32 + 255) / 256));
+  cudaStream_t st = hsd::as_stream(stream);
+  switch (x_dtype) {
+    case HSD_F32: return ssm_dispatch<float>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only, n_keep, rows);
+    case HSD_BF16: return ssm_dispatch<__nv_bfloat16>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only, n_keep, rows);
+  }
+  return hsd::set_error(HSD_ERR_DTYPE, "%s: x_dtype %d (f32 or bf16)", who, x_dtype);
+}
+
+}  // namespace
+
+extern "C" int hsd_mamba_conv_verify(const void* conv_in, int in_dtype, int64_t in_stride, const void* conv_state,
+                                     const void* w, int w_dtype, const void* bias, void* out, int out_dtype,
+                                     void* padded, int L, int C, int K, void* stream) {
+  return conv_impl("hsd_mamba_conv_verify", conv_in, in_dtype, in_stride, conv_state, w, w_dtype, bias, out,
+                   out_dtype, padded, L, C, K, nullptr, 0, stream);
 }
 
 extern "C" int hsd_mamba_ssm_verify(const void* xbc, int x_dtype, int64_t xbc_stride, const void* dt, int dt_dtype,
                                     int64_t dt_stride, const float* A_log, const float* D, const float* dt_bias,
                                     float dt_min, float dt_max, const float* state0, float* states, void* y,
                                     int y_dtype, int L, int H, int P, int G, int N, int last_only, void* stream) {
-  if (!xbc || !dt || !A_log || !D || !dt_bias || !states || !y)
-    return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_ssm_verify: null pointer");
-  if (L < 1 || H < 1 || P < 1 || G < 1 || H % G != 0 || xbc_stride < static_cast<int64_t>(H) * P + 2 * G * N)
-    return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_ssm_verify: bad shape (H %% G == 0, xbc_stride >= H*P + 2*G*N)");
-  if (!hsd::aligned(states, 16) || (state0 && !hsd::aligned(state0, 16)))
-    return hsd::set_error(HSD_ERR_ALIGN, "hsd_mamba_ssm_verify: states must be 16-byte aligned");
-  const int64_t warps = static_cast<int64_t>(H) * P;
-  dim3 grid(static_cast<unsigned>((warps * 32 + 255) / 256));
-  cudaStream_t st = hsd::as_stream(stream);
-  switch (x_dtype) {
-    case HSD_F32: return ssm_dispatch<float>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only);
-    case HSD_BF16: return ssm_dispatch<__nv_bfloat16>(dt_dtype, y_dtype, N, grid, st, xbc, xbc_stride, dt, dt_stride, A_log, D, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, last_only);
-  }
-  return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_ssm_verify: x_dtype %d (f32 or bf16)", x_dtype);
+  return ssm_impl("hsd_mamba_ssm_verify", xbc, x_dtype, xbc_stride, dt, dt_dtype, dt_stride, A_log, D, dt_bias,
+                  dt_min, dt_max, state0, states, y, y_dtype, L, H, P, G, N, last_only, nullptr, 0, stream);
+}
+
+extern "C" int hsd_mamba_conv_step(const void* conv_in, int in_dtype, int64_t in_stride, void* padded,
+                                   const int* n_keep, int rows, const void* w, int w_dtype, const void* bias,
+                                   void* out, int out_dtype, int L, int C, int K, void* stream) {
+  if (!n_keep || rows < 1 || L > rows)
+    return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_conv_step: need n_keep and 1 <= L <= rows (L=%d rows=%d)", L, rows);
+  return conv_impl("hsd_mamba_conv_step", conv_in, in_dtype, in_stride, nullptr, w, w_dtype, bias, out, out_dtype,
+                   padded, L, C, K, n_keep, rows, stream);
+}
+
+extern "C" int hsd_mamba_ssm_step(const void* xbc, int x_dtype, int64_t xbc_stride, const void* dt, int dt_dtype,
+                                  int64_t dt_stride, const float* A_log, const float* D, const float* dt_bias,
+                                  float dt_min, float dt_max, float* states, const int* n_keep, int rows, void* y,
+                                  int y_dtype, int L, int H, int P, int G, int N, void* stream) {
+  if (!n_keep || rows < 1 || L > rows)
+    return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_ssm_step: need n_keep and 1 <= L <= rows (L=%d rows=%d)", L, rows);
+  return ssm_impl("hsd_mamba_ssm_step", xbc, x_dtype, xbc_stride, dt, dt_dtype, dt_stride, A_log, D, dt_bias, dt_min,
+                  dt_max, nullptr, states, y, y_dtype, L, H, P, G, N, 0, n_keep, rows, stream);
 }
 
 extern "C" int hsd_mamba_rollback(const float* states, const void* padded, int elem_bytes, int n_keep, int L, int H,

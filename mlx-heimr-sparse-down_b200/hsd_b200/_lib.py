@@ -43,6 +43,13 @@ SIGNATURES = {
     "hsd_mamba_ssm_verify": [_P, _I, _L, _P, _I, _L, _P, _P, _P, ctypes.c_float, ctypes.c_float, _P, _P, _P,
                              _I, _I, _I, _I, _I, _I, _I, _P],
     "hsd_mamba_rollback": [_P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P],
+    "hsd_mamba_conv_step": [_P, _I, _L, _P, _P, _I, _P, _I, _P, _P, _I, _I, _I, _I, _P],
+    "hsd_mamba_ssm_step": [_P, _I, _L, _P, _I, _L, _P, _P, _P, ctypes.c_float, ctypes.c_float, _P, _P, _I, _P,
+                           _I, _I, _I, _I, _I, _I, _P],
+    "hsd_moe_up_decode": [_P, _I, _L, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
+    "hsd_qlinear_decode": [_P, _I, _L, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P],
+    "hsd_dense_down_decode": [_P, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I,
+                              _I, _P],
     "hsd_prefill_noalloc_max_bytes": [_P],
     "hsd_sparse_down_prefill_noalloc": [_P, _I, _P, _P, _P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I,
                                         _I, _I, _I, _I, _I, _I, _P],

@@ -77,3 +77,36 @@ def live_rows(h, *, F, FS, topk):
         _lib.call("hsd_decode_live_rows", _lib.ptr(h), _lib.dtype_code(h, "live_rows"), _lib.ptr(live),
                   _lib.ptr(count), B, F, FS, topk, _lib.stream_of(h))
     return live, count
+
+
+def dense_down(h, sel, gains, w, s, b, sw, ss, sb, *, F, FS, D, topk, out_dtype=None, resid=None, out=None,
+               workspace=None):
+    """The stock dense down projection (hsd/model.py:132-133 decode_dense) on the checkpoint
+    layout: every weight of the selected experts, fp32 accumulation, the slot partials summed
+    in slot order. w [E, D, F/8] / s, b [E, D, F/64]; sw [D, FS/8] / ss, sb [D, FS/64]; the
+    other arguments as sparse_down. workspace: fp32 [B, topk+1, D] (allocated when None)."""
+    what = "dense_down"
+    _lib.require_cuda(h, sel, gains, w, s, b, sw, ss, sb, resid, out, workspace, what=what)
+    B = h.shape[0]
+    E = w.shape[0] if topk > 0 else 0
+    if h.shape[1] != topk * F + FS or tuple(gains.shape) != (B, topk + 1) or gains.dtype != torch.float32:
+        raise ValueError(f"{what}: h must be [B, topk*F+FS] and gains float32 [B, topk+1]")
+    if topk > 0 and (tuple(w.shape) != (E, D, F // 8) or tuple(s.shape) != (E, D, F // 64)):
+        raise ValueError(f"{what}: routed weights {tuple(w.shape)} do not match the checkpoint layout [E, D, F/8]")
+    if FS > 0 and (tuple(sw.shape) != (D, FS // 8) or tuple(ss.shape) != (D, FS // 64)):
+        raise ValueError(f"{what}: shared weights do not match [D, FS/8]")
+    sref = s if topk > 0 else ss
+    od = out_dtype or h.dtype
+    if out is None:
+        out = torch.empty((B, D), dtype=od, device=h.device)
+    if workspace is None:
+        workspace = torch.empty((B, topk + 1, D), dtype=torch.float32, device=h.device)
+    elif workspace.numel() < B * (topk + 1) * D or workspace.dtype != torch.float32:
+        raise ValueError(f"{what}: workspace must hold {B * (topk + 1) * D} fp32")
+    if B == 0:
+        return out
+    _lib.call("hsd_dense_down_decode", _lib.ptr(h), _lib.dtype_code(h, what), _lib.ptr(sel), _lib.ptr(gains),
+              _lib.ptr(w), _lib.ptr(s), _lib.ptr(b), _lib.dtype_code(sref, what), _lib.ptr(sw), _lib.ptr(ss),
+              _lib.ptr(sb), _lib.ptr(resid), _lib.ptr(out), _lib.dtype_code(out, what), _lib.ptr(workspace),
+              B, D, F, FS, topk, E, _lib.stream_of(h))
+    return out

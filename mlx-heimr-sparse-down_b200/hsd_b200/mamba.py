@@ -160,6 +160,80 @@ def mamba_rollback(records, n_keep):
         cache[1] = states[n_keep - 1]
 
 
+def conv_step(conv_in, padded, n_keep, conv_w, conv_b, out_dtype=torch.bfloat16):
+    """Resident-buffer conv: the window is padded[n_keep .. n_keep+K-2] (n_keep a device int32
+    tensor holding the previous call's kept row count); padded [rows + K-1, C] receives the
+    window and the L new rows in place. -> silu(conv) [L, C]."""
+    L, C = conv_in.shape
+    K = conv_w.shape[1]
+    rows = padded.shape[0] - (K - 1)
+    if conv_in.stride(1) != 1 or not padded.is_contiguous() or padded.dtype != conv_in.dtype:
+        raise ValueError("conv_step: conv_in rows and padded must be contiguous, padded in conv_in's dtype")
+    out = torch.empty((L, C), dtype=out_dtype, device=conv_in.device)
+    _lib.call("hsd_mamba_conv_step", _lib.ptr(conv_in), _lib.dtype_code(conv_in, "conv_in"), conv_in.stride(0),
+              _lib.ptr(padded), _lib.ptr(n_keep), rows, _lib.ptr(conv_w), _lib.dtype_code(conv_w, "conv_w"),
+              _lib.ptr(conv_b), _lib.ptr(out), _lib.dtype_code(out, "out"), L, C, K, _lib.stream_of(conv_in))
+    return out
+
+
+def ssm_step(xbc, dt, A_log, D, dt_bias, states, n_keep, *, H, P, G, N, time_step_limit=(0.0, float("inf")),
+             y_dtype=torch.float32):
+    """Resident-buffer selective scan: the state is states[n_keep-1] (n_keep a device int32
+    tensor), and the state after each of the L rows is written to states[0 .. L-1] in place
+    (states [rows, H, P, N] fp32). -> y [L, H*P]."""
+    L = xbc.shape[0]
+    if xbc.stride(1) != 1 or dt.stride(1) != 1 or not states.is_contiguous() or states.dtype != torch.float32:
+        raise ValueError("ssm_step: rows must be contiguous and states fp32 contiguous")
+    y = torch.empty((L, H * P), dtype=y_dtype, device=xbc.device)
+    lo, hi = time_step_limit
+    _lib.call("hsd_mamba_ssm_step", _lib.ptr(xbc), _lib.dtype_code(xbc, "xbc"), xbc.stride(0), _lib.ptr(dt),
+              _lib.dtype_code(dt, "dt"), dt.stride(0), _lib.ptr(A_log), _lib.ptr(D), _lib.ptr(dt_bias), float(lo),
+              float(hi), _lib.ptr(states), _lib.ptr(n_keep), states.shape[0], _lib.ptr(y), _lib.dtype_code(y, "y"),
+              L, H, P, G, N, _lib.stream_of(xbc))
+    return y
+
+
+class ResidentMambaCache:
+    """A Mamba-2 layer's decode state in fixed buffers, for graph-replayed decode loops:
+    padded [rows + K-1, conv_dim] (the conv window and the last call's rows) and states
+    [rows, H, P, N] (the state after each row of the last call). The kept row count lives in
+    one device int32 shared by all layers of a model (`n_keep`), so a rollback after a verify
+    is a single device write."""
+
+    def __init__(self, block, rows, device, dtype=torch.bfloat16):
+        self.rows = rows
+        self.padded = torch.zeros((rows + block.K - 1, block.conv_dim), dtype=dtype, device=device)
+        self.states = torch.zeros((rows, block.H, block.P, block.N), dtype=torch.float32, device=device)
+
+    def load(self, cache, n_keep_host=1):
+        """Seed from an ArraysCache-style [conv window [K-1, C], state [H, P, N]] (prefill's
+        result): window to padded[n_keep .. n_keep+K-2], state to states[n_keep-1]."""
+        conv, st = cache
+        k = n_keep_host
+        self.padded.zero_()
+        self.states.zero_()
+        if conv is not None:
+            self.padded[k:k + conv.shape[0]].copy_(conv)
+        if st is not None:
+            self.states[k - 1].copy_(st)
+
+
+def mamba_step_resident(block, x, rc, n_keep):
+    """One Mamba-2 block on x [L, D] (L <= rc.rows) over a ResidentMambaCache: the conv window
+    and state come from the previous call's rows selected by n_keep, and every row's state is
+    kept for a later rollback. Graph-capturable (no host reads, fixed buffers).
+    Returns x + mixer(norm(x))."""
+    b = block
+    I, Cd = b.I, b.conv_dim
+    h = rms_norm(x, b.norm_w, b.eps)
+    proj = h @ b.in_proj.t()
+    co = conv_step(proj[:, I:I + Cd], rc.padded, n_keep, b.conv_w, b.conv_b)
+    y = ssm_step(co, proj[:, I + Cd:], b.A_log, b.D, b.dt_bias, rc.states, n_keep, H=b.H, P=b.P, G=b.G, N=b.N,
+                 time_step_limit=b.time_step_limit)
+    yn = gated_rms_norm(y, proj[:, :I], b.gate_norm_w, I // b.G, b.eps, x.dtype)
+    return x + yn @ b.out_proj.t()
+
+
 def rollback_into(padded, states, n_keep, conv_out, state_out):
     """The rollback as copies into fixed buffers (for callers whose cache tensors must keep
     their addresses, e.g. a captured CUDA graph): conv_out [K-1, C] <- padded[n_keep:],

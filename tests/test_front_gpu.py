@@ -1,0 +1,140 @@
+"""The fused 4-bit matrix-vector kernels of the decode step on the GPU against the oracle:
+
+  moe_up      the MoE front end's up projections + relu2 (hsd/model.py:110-121) vs
+              oracle/front.py (fp32 dequantised weights, numpy matmul)
+  dense_down  the stock dense down projection (hsd/model.py:132-133) vs the C oracle's fp32
+              dequantised reference (the same one the sparse kernel is checked against)
+
+Bars: 1e-3 of max|ref| for fp32 outputs (fp32 accumulation both sides, different order),
+1e-2 for bf16 outputs (one bf16 rounding); an expert id outside [0, E) gives zeros for its
+slot and HSD_ERR_INDEX in the device status word."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import bits16_np, f32_np, rel_err, words_np
+from oracle import cport
+from oracle import front as ofront
+from oracle.quant import bf16_bits_to_f32
+
+import hsd_b200
+from hsd_b200 import synth
+from hsd_b200.decode import dense_down
+from hsd_b200.front import moe_up
+
+TOL32 = 1e-3
+TOL16 = 1e-2
+
+
+def up_case(seed, B, D, F, FS, E, topk, device):
+    gen = torch.Generator(device=device).manual_seed(seed)
+    uw, us, ub = synth.quantized_weights((E, F, D), gen, device)
+    suw, sus, sub = synth.quantized_weights((FS, D), gen, device) if FS else (None, None, None)
+    x = torch.randn((B, D), generator=gen, device=device).to(torch.bfloat16)
+    logits = torch.randn((B, E), generator=gen, device=device)
+    sel, _ = synth.route_topk(logits, topk) if topk else (torch.zeros((B, 0), dtype=torch.int32, device=device), None)
+    return x, sel.to(torch.int32).contiguous(), (uw, us, ub), (suw, sus, sub)
+
+
+def oracle_up(x, sel, up, sup, topk):
+    uw, us, ub = up
+    suw, sus, sub = sup
+    f = lambda t: bf16_bits_to_f32(bits16_np(t)) if t is not None else None  # noqa: E731
+    return ofront.moe_up(f32_np(x), sel.cpu().numpy(), words_np(uw) if uw is not None else None, f(us), f(ub),
+                         words_np(suw) if suw is not None else None, f(sus), f(sub), topk=topk)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,D,F,FS,E,topk", [(1, 2688, 1856, 3712, 128, 6), (3, 2688, 1856, 3712, 128, 6),
+                                              (5, 384, 256, 512, 16, 4), (2, 4096, 128, 64, 4, 2)])
+def test_moe_up_vs_oracle(cuda, B, D, F, FS, E, topk):
+    x, sel, up, sup = up_case(7 + B, B, D, F, FS, E, topk, cuda)
+    ref = oracle_up(x, sel, up, sup, topk)
+    h32 = moe_up(x, sel, *up, *sup, F=F, FS=FS, D=D, topk=topk, out_dtype=torch.float32)
+    h16 = moe_up(x, sel, *up, *sup, F=F, FS=FS, D=D, topk=topk)
+    assert rel_err(f32_np(h32), ref) < TOL32
+    assert rel_err(f32_np(h16), ref) < TOL16
+    assert float(h32.min()) >= 0.0
+    assert hsd_b200.device_status() == 0
+
+
+@pytest.mark.gpu
+def test_moe_up_strided_rows_and_forms(cuda):
+    """x rows with a stride (a view into a wider buffer), the shared-only (topk = 0) and the
+    routed-only (FS = 0) forms."""
+    B, D, F, FS, E, topk = 3, 384, 256, 512, 8, 3
+    x, sel, up, sup = up_case(21, B, D, F, FS, E, topk, cuda)
+    wide = torch.zeros((B, D + 64), dtype=x.dtype, device=cuda)
+    wide[:, 32:32 + D] = x
+    xv = wide[:, 32:32 + D]
+    ref = oracle_up(x, sel, up, sup, topk)
+    h = moe_up(xv, sel, *up, *sup, F=F, FS=FS, D=D, topk=topk, out_dtype=torch.float32)
+    assert rel_err(f32_np(h), ref) < TOL32
+    hs = moe_up(x, None, None, None, None, *sup, F=F, FS=FS, D=D, topk=0, out_dtype=torch.float32)
+    assert rel_err(f32_np(hs), ref[:, topk * F:]) < TOL32
+    hr = moe_up(x, sel, *up, None, None, None, F=F, FS=0, D=D, topk=topk, out_dtype=torch.float32)
+    assert rel_err(f32_np(hr), ref[:, :topk * F]) < TOL32
+
+
+@pytest.mark.gpu
+def test_moe_up_bad_expert_id_is_zero_and_flagged(cuda):
+    B, D, F, FS, E, topk = 2, 384, 256, 512, 8, 2
+    x, sel, up, sup = up_case(5, B, D, F, FS, E, topk, cuda)
+    hsd_b200.device_status()
+    sel[1, 0] = E + 3
+    h = moe_up(x, sel, *up, *sup, F=F, FS=FS, D=D, topk=topk, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert float(h[1, :F].abs().max()) == 0.0
+    assert hsd_b200.device_status() == hsd_b200._lib.HSD_ERR_INDEX
+    assert hsd_b200.device_status() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,z", [(1, 0.9), (3, 0.8), (8, 0.97)])
+def test_dense_down_vs_oracle(cuda, B, z):
+    c = synth.decode_case(seed=300 + B, B=B, zero_frac=z, device=cuda)
+    ref = cport.dense_down(f32_np(c["h"]), c["sel"].cpu().numpy(), c["gains"].cpu().numpy(), words_np(c["w"]),
+                           bits16_np(c["s"]), bits16_np(c["b"]), words_np(c["sw"]), bits16_np(c["ss"]),
+                           bits16_np(c["sb"]), F=c["F"], FS=c["FS"], D=c["D"], topk=c["topk"])
+    y = dense_down(c["h"], c["sel"], c["gains"], c["w"], c["s"], c["b"], c["sw"], c["ss"], c["sb"], F=c["F"],
+                   FS=c["FS"], D=c["D"], topk=c["topk"], out_dtype=torch.float32)
+    assert rel_err(f32_np(y), ref) < TOL32
+    # with the residual, rounded once to bf16
+    resid = torch.randn((B, c["D"]), device=cuda).to(torch.bfloat16)
+    yr = dense_down(c["h"], c["sel"], c["gains"], c["w"], c["s"], c["b"], c["sw"], c["ss"], c["sb"], F=c["F"],
+                    FS=c["FS"], D=c["D"], topk=c["topk"], resid=resid)
+    assert rel_err(f32_np(yr), f32_np(resid) + ref) < TOL16
+    assert hsd_b200.device_status() == 0
+
+
+@pytest.mark.gpu
+def test_dense_and_sparse_down_agree(cuda):
+    """The two down projections on the same inputs (checkpoint vs neuron-major layout): fp32
+    accumulation in different orders, so they agree to fp32 rounding, not bit for bit."""
+    c = synth.decode_case(seed=311, B=3, zero_frac=0.9, device=cuda)
+    pw, ps, pb = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"])
+    spw, sps, spb = hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
+    ys = hsd_b200.sparse_down(c["h"], c["sel"], c["gains"], pw, ps, pb, spw, sps, spb, F=c["F"], FS=c["FS"],
+                              D=c["D"], topk=c["topk"], out_dtype=torch.float32)
+    yd = dense_down(c["h"], c["sel"], c["gains"], c["w"], c["s"], c["b"], c["sw"], c["ss"], c["sb"], F=c["F"],
+                    FS=c["FS"], D=c["D"], topk=c["topk"], out_dtype=torch.float32)
+    assert rel_err(f32_np(ys), f32_np(yd)) < 1e-5
+    assert np.isfinite(f32_np(yd)).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,in_f,out_f", [(1, 2688, 10304), (3, 4096, 2688), (2, 5376, 2688), (4, 8192, 96),
+                                          (1, 64, 40)])
+def test_qlinear_vs_oracle(cuda, B, in_f, out_f):
+    from oracle.quant import dequantize
+    from hsd_b200.front import qlinear
+    gen = torch.Generator(device=cuda).manual_seed(in_f + out_f + B)
+    w, s, b = synth.quantized_weights((out_f, in_f), gen, cuda)
+    x = torch.randn((B, in_f), generator=gen, device=cuda).to(torch.bfloat16)
+    Wf = dequantize(words_np(w), bf16_bits_to_f32(bits16_np(s)), bf16_bits_to_f32(bits16_np(b)))
+    ref = f32_np(x) @ Wf.T
+    y32 = qlinear(x, w, s, b, out_dtype=torch.float32)
+    assert rel_err(f32_np(y32), ref) < TOL32
+    resid = torch.randn((B, out_f), generator=gen, device=cuda).to(torch.bfloat16)
+    y16 = qlinear(x, w, s, b, resid=resid)
+    assert rel_err(f32_np(y16), f32_np(resid) + ref) < TOL16

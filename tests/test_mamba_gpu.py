@@ -129,3 +129,61 @@ def test_long_chunk_final_state_only(cuda):
     out, padded = hm.conv_verify(conv_in, None, w, None, out_dtype=torch.float32)
     oout, opad = om.conv_rows(f32_np(conv_in), None, f32_np(w), None)
     assert np.array_equal(f32_np(padded), opad) and rel_err(f32_np(out), oout) < 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("accepts", [[0, 2, 1, 2], [2, 2, 0, 0]])
+def test_resident_buffers_match_the_verify_rollback_path(cuda, accepts):
+    """The graph-friendly form (conv / scan in place over fixed buffers, the rollback one
+    device integer) against mamba_verify + mamba_rollback: a prefill, then verifies of 3 rows
+    each followed by a rollback to the accepted prefix -- every output and the final state
+    bit-identical."""
+    blk = hm.random_mamba2(seed=4, hidden=512, H=16, P=32, G=4, N=64, device=cuda)
+    gen = torch.Generator(device=cuda).manual_seed(9)
+    x0 = torch.randn((1, 7, 512), generator=gen, device=cuda).to(torch.bfloat16)
+    cache = [None, None]
+    hm.mamba_verify(blk, x0, cache, [], checkpoints=False)
+    rc = hm.ResidentMambaCache(blk, rows=3, device=cuda)
+    rc.load(cache)
+    n_keep = torch.ones(1, dtype=torch.int32, device=cuda)
+    for step, a in enumerate(accepts):
+        x = torch.randn((1, 3, 512), generator=gen, device=cuda).to(torch.bfloat16)
+        rec = []
+        ref = hm.mamba_verify(blk, x, cache, rec)[0]
+        out = hm.mamba_step_resident(blk, x[0], rc, n_keep)
+        assert torch.equal(out, ref), f"verify {step}: outputs differ"
+        hm.mamba_rollback(rec, a + 1)
+        n_keep.fill_(a + 1)
+    assert torch.equal(rc.states[n_keep.item() - 1], cache[1])
+    k = n_keep.item()
+    assert torch.equal(rc.padded[k:k + blk.K - 1], cache[0])
+    assert hm._lib.lib() is not None
+
+
+@pytest.mark.gpu
+def test_resident_single_steps_match_plain_steps(cuda):
+    """A plain decode step is the resident form with L = 1 and n_keep = 1."""
+    blk = hm.random_mamba2(seed=5, hidden=512, H=16, P=32, G=4, N=64, device=cuda)
+    gen = torch.Generator(device=cuda).manual_seed(11)
+    cache = [None, None]
+    rc = hm.ResidentMambaCache(blk, rows=3, device=cuda)
+    n_keep = torch.ones(1, dtype=torch.int32, device=cuda)
+    for _ in range(5):
+        x = torch.randn((1, 1, 512), generator=gen, device=cuda).to(torch.bfloat16)
+        ref = hm.mamba_verify(blk, x, cache, [])[0]
+        out = hm.mamba_step_resident(blk, x[0], rc, n_keep)
+        assert torch.equal(out, ref)
+    assert torch.equal(rc.states[0], cache[1])
+
+
+@pytest.mark.gpu
+def test_resident_bad_keep_is_flagged(cuda):
+    import hsd_b200
+    blk = hm.random_mamba2(seed=6, hidden=512, H=16, P=32, G=4, N=64, device=cuda)
+    rc = hm.ResidentMambaCache(blk, rows=3, device=cuda)
+    hsd_b200.device_status()
+    n_keep = torch.full((1,), 9, dtype=torch.int32, device=cuda)
+    x = torch.randn((1, 512), device=cuda).to(torch.bfloat16)
+    hm.mamba_step_resident(blk, x, rc, n_keep)
+    torch.cuda.synchronize()
+    assert hsd_b200.device_status() == hsd_b200._lib.HSD_ERR_INDEX
