@@ -100,6 +100,19 @@ int hsd_sparse_down_decode(const void* h, int h_dtype, const int32_t* sel,
                            int y_dtype, int B, int D, int F, int FS, int topk, int E,
                            int loadsc, void* stream);
 
+/* The dense form of the same kernel: every row of the selected experts is read (the
+ * down projection of hsd/model.py:132-133 decode_dense) on the neuron-major layout, with
+ * the sparse kernel's own fixed reduction order -- a row whose h is zero adds an exact zero
+ * where the sparse form skips it, so hsd_sparse_down_decode reproduces this output bit for
+ * bit on any input. No counterpart in the reference (its dense path is mlx-lm's stock
+ * gather_qmm); it is the exact-parity reference of the sparse form. Same arguments as
+ * hsd_sparse_down_decode without loadsc. */
+int hsd_dense_down_decode_nm(const void* h, int h_dtype, const int32_t* sel, const float* gains,
+                             const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
+                             const uint32_t* spw, const void* sps, const void* spb,
+                             const void* resid, void* y, int y_dtype, int B, int D, int F, int FS,
+                             int topk, int E, void* stream);
+
 /* The active-index sets of the decode kernel (hsd/decode.py:86-101): per (token, slot),
  * slot < topk routed and slot == topk the shared expert, the ascending indices of the
  * nonzero h entries, compacted by the same warp-ballot routine the decode kernel runs.
@@ -241,6 +254,31 @@ int hsd_dense_down_decode(const void* h, int h_dtype, const int32_t* sel, const 
 int hsd_qlinear_decode(const void* x, int x_dtype, int64_t x_stride, const uint32_t* w, const void* s,
                        const void* b, int s_dtype, const void* resid, void* y, int y_dtype, int B,
                        int in_f, int out_f, void* stream);
+
+/* ---- per-row operators of the decode step (the model around the hot path) --------- */
+
+/* RMSNorm as NemotronH applies it (mlx.fast.rms_norm in the reference's model): per row
+ * y = w * cast(x * rsqrt(mean(x^2) + eps)), the normalised row rounded to x's dtype before
+ * the weight multiply, fp32 arithmetic. x [B, D] with row stride x_stride; y [B, D]. */
+int hsd_rms_norm(const void* x, int x_dtype, int64_t x_stride, const void* w, int w_dtype, void* y,
+                 int y_dtype, int B, int D, float eps, void* stream);
+
+/* The Mamba-2 mixer's gated norm: g = y * silu(gate), per group of `group` channels
+ * out = w * cast(g * rsqrt(mean(g^2) + eps)). y [B, I] (row stride y_stride), gate [B, I]
+ * (row stride g_stride), out [B, I] contiguous. I % group == 0. */
+int hsd_gated_rms_norm(const void* y, int y_dtype, int64_t y_stride, const void* gate, int g_dtype,
+                       int64_t g_stride, const void* w, int w_dtype, void* out, int out_dtype, int B,
+                       int I, int group, float eps, void* stream);
+
+/* The MoE router (hsd/model.py:115, the block's gate): scores = sigmoid(x . R_e) in fp32 for
+ * R [E, D] fp32, the top-k experts by score (ties to the lower id) -> sel [B, topk] int32 and
+ * gains [B, topk+1] f32 = the scores over their sum, then 1 for the shared expert.
+ * scores [B, E] fp32 is scratch; ticket is one caller-owned unsigned int, zero before the
+ * first call and reset by every call (calls sharing a ticket must not overlap).
+ * 1 <= topk <= min(E, 16), E <= 1024, B <= 65535. */
+int hsd_router_topk(const void* x, int x_dtype, int64_t x_stride, const float* R, int B, int D, int E,
+                    int topk, float* scores, unsigned int* ticket, int32_t* sel, float* gains,
+                    void* stream);
 
 /* ---- allocation-free prefill ------------------------------------------------------ */
 

@@ -73,6 +73,7 @@ struct DecodeParams {
   const void* resid;
   void* y;
   int B, D, F, FS, topk, E, loadsc;
+  int all_rows;   // 1: every row of the selected experts is live (the dense form)
   int NR;    // columns of h: topk*F + FS
   int GT;    // groups per token
   int NW;    // words per neuron row: D/8
@@ -249,7 +250,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
       const bool valid = S.gsrc[gi] != -2;
       const float v0 = valid ? S.hs[gi * kGS + lane] : 0.f;
       const float v1 = valid ? S.hs[gi * kGS + 32 + lane] : 0.f;
-      const unsigned long long m = ballot64(v0 != 0.f, v1 != 0.f);
+      const unsigned long long m = p.all_rows ? ballot64(valid, valid) : ballot64(v0 != 0.f, v1 != 0.f);
       if (lane == 0) {
         S.gmask[gi] = m;
         S.gcnt[gi] = __popcll(m);
@@ -265,7 +266,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
     __syncthreads();
     // ---- 3. the counts' exclusive scan (every warp, redundantly), the compaction and the
     //         row copies of the first sub-batch
-    int nrows;
+    int nrows, first_rows;
     {
       const int c = (lane < ng) ? S.gcnt[lane] : 0;
       int x = c;
@@ -276,6 +277,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
       }
       const int goff_lane = x - c;
       nrows = __shfl_sync(0xffffffffu, x, 31);
+      // sub-batches end on group boundaries (the last group start or end <= RB), so no
+      // group is ever folded in two pieces: a group's sum is the same sequence of fp32
+      // operations whatever the other groups' live counts, and the dense form (all rows
+      // live, zeros included) reproduces the sparse form bit for bit
+      const unsigned cand = (lane < ng && goff_lane <= RB) ? static_cast<unsigned>(goff_lane) : 0u;
+      const unsigned first_end = max(__reduce_max_sync(0xffffffffu, cand),
+                                     nrows <= RB ? static_cast<unsigned>(nrows) : 0u);
+      first_rows = static_cast<int>(first_end);
       if (warp == 0) {
         if (lane < ng) S.goff[lane] = goff_lane;
         if (lane == 0) S.goff[ng] = nrows;
@@ -284,7 +293,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
         const unsigned live_groups = __popc(__ballot_sync(0xffffffffu, c > 0));
         if (lane == 0 && nrows > 0)
           mbar_arrive_expect_tx(bar, (p.loadsc ? live_groups * 2u * meta_bytes : 0u) +
-                                         static_cast<uint32_t>(min(nrows, RB)) * row_bytes);
+                                         first_end * row_bytes);
       }
       for (int gi = warp; gi < ng; gi += WARPS) {
         const unsigned long long m = S.gmask[gi];
@@ -300,16 +309,24 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
             const int idx = base + live_prefix(m, j);
             S.rows[idx] = static_cast<uint16_t>((gi << 6) | j);
             S.hrow[idx] = S.hs[gi * kGS + j];
-            if (idx < RB) bulk_g2s(&S.stage[idx * NWC], wbase + (rowbase + j) * p.NW + w0, row_bytes, bar, pol);
+            if (idx < first_rows) bulk_g2s(&S.stage[idx * NWC], wbase + (rowbase + j) * p.NW + w0, row_bytes, bar, pol);
           }
         }
       }
     }
     __syncthreads();
 
-    // ---- 4. per sub-batch of RB rows: wait for the copies, accumulate from shared memory
-    for (int r0 = 0; r0 < nrows; r0 += RB) {
-      const int rn = min(RB, nrows - r0);
+    // ---- 4. per sub-batch of at most RB rows and whole groups: wait for the copies,
+    //         accumulate from shared memory
+    for (int r0 = 0, r1 = first_rows; r0 < nrows; r0 = r1) {
+      if (r0 > 0) {                              // the next group boundary within RB rows
+        r1 = r0;
+        for (int g = 0; g <= ng; ++g) {
+          const int o = S.goff[g];
+          if (o > r1 && o - r0 <= RB) r1 = o;
+        }
+      }
+      const int rn = r1 - r0;
       if (r0 > 0) {                              // later sub-batches (dense h only)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         if (tid == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(rn) * row_bytes);
@@ -348,8 +365,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
             acc[6] = fmaf(hv, nib_unit<6>(q), acc[6]);
             acc[7] = fmaf(hv, nib_unit<7>(q), acc[7]);
           }
-          // the affine form is linear in the row set, so a group split across
-          // sub-batches is folded in piece by piece
           const float g = S.ggain[gi];
           if (p.loadsc) {
             const uint4 s4 = *reinterpret_cast<const uint4*>(&S.meta_s[gi * C + wp * 8]);
@@ -484,15 +499,18 @@ int launch_decode(const DecodeParams& p, cudaStream_t st) {
 }
 
 // Output chunk width (outputs per cluster): 192 (112 CTAs per token, one per SM) for
-// B <= 2, where a token's CTAs should not share SMs; 128 (168 CTAs per token) above.
+// B <= 4, where a token's CTAs should not share SMs; 128 (168 CTAs per token) above.
 // HSD_DECODE_CHUNK=128 or 192 forces one for tuning.
+// A token's arithmetic depends on the chunk width only (its groups' lane assignment), so
+// the widths of B = 1 and of verify steps up to 4 rows are the same: a verify row equals the
+// same token decoded alone, bit for bit.
 inline int chunk_choice(int B) {
   static int forced = [] {
     const char* e = getenv("HSD_DECODE_CHUNK");
     return e ? atoi(e) : 0;
   }();
   if (forced == 128 || forced == 192) return forced;
-  return B <= 2 ? 192 : 128;
+  return B <= 4 ? 192 : 128;
 }
 
 template <typename HT, typename ST, typename YT>
@@ -521,12 +539,12 @@ int dispatch_s(int s_dtype, int y_dtype, const DecodeParams& p, cudaStream_t st)
 
 }  // namespace
 
-extern "C" int hsd_sparse_down_decode(const void* h, int h_dtype, const int32_t* sel,
-                                      const float* gains, const uint32_t* pw, const void* ps,
-                                      const void* pb, int s_dtype, const uint32_t* spw,
-                                      const void* sps, const void* spb, const void* resid, void* y,
-                                      int y_dtype, int B, int D, int F, int FS, int topk, int E,
-                                      int loadsc, void* stream) {
+namespace {
+
+int decode_impl(const void* h, int h_dtype, const int32_t* sel, const float* gains, const uint32_t* pw,
+                const void* ps, const void* pb, int s_dtype, const uint32_t* spw, const void* sps, const void* spb,
+                const void* resid, void* y, int y_dtype, int B, int D, int F, int FS, int topk, int E, int loadsc,
+                int all_rows, void* stream) {
   // topk == 0: the shared expert alone; FS == 0: routed experts alone (the forms the
   // expert-parallel exchange uses); the pointers of an absent part may be NULL
   if (!h || !gains || !y) return hsd::set_error(HSD_ERR_ARG, "hsd_sparse_down_decode: null pointer");
@@ -554,6 +572,7 @@ extern "C" int hsd_sparse_down_decode(const void* h, int h_dtype, const int32_t*
   p.spw = spw; p.sps = static_cast<const uint16_t*>(sps); p.spb = static_cast<const uint16_t*>(spb);
   p.resid = resid; p.y = y;
   p.B = B; p.D = D; p.F = F; p.FS = FS; p.topk = topk; p.E = E; p.loadsc = loadsc ? 1 : 0;
+  p.all_rows = all_rows ? 1 : 0;
   p.NR = static_cast<int>(NR);
   p.GT = topk * (F / kGS) + FS / kGS;
   p.NW = D / 8;
@@ -564,6 +583,27 @@ extern "C" int hsd_sparse_down_decode(const void* h, int h_dtype, const int32_t*
     case HSD_BF16: return dispatch_s<__nv_bfloat16>(s_dtype, y_dtype, p, st);
   }
   return hsd::set_error(HSD_ERR_DTYPE, "hsd_sparse_down_decode: h_dtype %d", h_dtype);
+}
+
+}  // namespace
+
+extern "C" int hsd_sparse_down_decode(const void* h, int h_dtype, const int32_t* sel,
+                                      const float* gains, const uint32_t* pw, const void* ps,
+                                      const void* pb, int s_dtype, const uint32_t* spw,
+                                      const void* sps, const void* spb, const void* resid, void* y,
+                                      int y_dtype, int B, int D, int F, int FS, int topk, int E,
+                                      int loadsc, void* stream) {
+  return decode_impl(h, h_dtype, sel, gains, pw, ps, pb, s_dtype, spw, sps, spb, resid, y, y_dtype, B, D, F, FS,
+                     topk, E, loadsc, 0, stream);
+}
+
+extern "C" int hsd_dense_down_decode_nm(const void* h, int h_dtype, const int32_t* sel, const float* gains,
+                                        const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
+                                        const uint32_t* spw, const void* sps, const void* spb, const void* resid,
+                                        void* y, int y_dtype, int B, int D, int F, int FS, int topk, int E,
+                                        void* stream) {
+  return decode_impl(h, h_dtype, sel, gains, pw, ps, pb, s_dtype, spw, sps, spb, resid, y, y_dtype, B, D, F, FS,
+                     topk, E, 1, 1, stream);
 }
 
 extern "C" int hsd_decode_live_rows(const void* h, int h_dtype, int32_t* live, int32_t* count, int B,

@@ -32,6 +32,8 @@ SIGNATURES = {
     "hsd_swap_last2_u16": [_P, _P, _L, _L, _L, _P],
     "hsd_sparse_down_decode": [_P, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I,
                                _I, _I, _I, _I, _I, _I, _I, _P],
+    "hsd_dense_down_decode_nm": [_P, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I,
+                                 _I, _I, _I, _I, _I, _I, _P],
     "hsd_decode_live_rows": [_P, _I, _P, _P, _I, _I, _I, _I, _P],
     "hsd_prefill_num_tiles": [_I, _I, _I, _I, _P, _P],
     "hsd_prefill_build_tiles": [_P, _I, _I, _I, _I, _P, _P, _P],
@@ -48,6 +50,9 @@ SIGNATURES = {
                            _I, _I, _I, _I, _I, _I, _P],
     "hsd_moe_up_decode": [_P, _I, _L, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
     "hsd_qlinear_decode": [_P, _I, _L, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P],
+    "hsd_rms_norm": [_P, _I, _L, _P, _I, _P, _I, _I, _I, ctypes.c_float, _P],
+    "hsd_gated_rms_norm": [_P, _I, _L, _P, _I, _L, _P, _I, _P, _I, _I, _I, _I, ctypes.c_float, _P],
+    "hsd_router_topk": [_P, _I, _L, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P],
     "hsd_dense_down_decode": [_P, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I,
                               _I, _P],
     "hsd_prefill_noalloc_max_bytes": [_P],

@@ -12,7 +12,7 @@ from . import _lib
 
 
 def sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D, topk,
-                sl=928, unr=2, nds=3, out_dtype=None, loadsc=1, resid=None, out=None):
+                sl=928, unr=2, nds=3, out_dtype=None, loadsc=1, resid=None, out=None, all_rows=False):
     """hsd/decode.py:238 -- the down projection over the live rows only.
 
     h [B, topk*F + FS] (bf16 / f16 / f32), sel [B, topk] int32 (the routed experts),
@@ -23,7 +23,9 @@ def sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D, topk,
     sl / unr / nds are the Metal kernel's tuning knobs; they are accepted for signature
     parity and have no effect here. loadsc=0 skips the scale / bias loads (benchmark-only,
     as in the reference). resid [B, D] (out dtype), when given, is added in the kernel
-    (y = resid + down(h)); out, when given, receives y.
+    (y = resid + down(h)); out, when given, receives y. all_rows=True is the dense form
+    (hsd_dense_down_decode_nm): every row read, the same reduction order, so the sparse form
+    reproduces it bit for bit.
     """
     del sl, unr, nds
     what = "sparse_down"
@@ -57,6 +59,12 @@ def sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D, topk,
     if resid is not None and (resid.dtype != od or tuple(resid.shape) != (B, D)):
         raise ValueError(f"{what}: resid must be {od} [{B}, {D}]")
     if B == 0:
+        return out
+    if all_rows:
+        _lib.call("hsd_dense_down_decode_nm", _lib.ptr(h), _lib.dtype_code(h, what), _lib.ptr(sel),
+                  _lib.ptr(gains), _lib.ptr(pw), _lib.ptr(ps), _lib.ptr(pb), _lib.dtype_code(sref, what),
+                  _lib.ptr(spw), _lib.ptr(sps), _lib.ptr(spb), _lib.ptr(resid), _lib.ptr(out),
+                  _lib.dtype_code(out, what), B, D, F, FS, topk, E, _lib.stream_of(h))
         return out
     _lib.call("hsd_sparse_down_decode", _lib.ptr(h), _lib.dtype_code(h, what), _lib.ptr(sel),
               _lib.ptr(gains), _lib.ptr(pw), _lib.ptr(ps), _lib.ptr(pb), _lib.dtype_code(sref, what),

@@ -166,3 +166,33 @@ def test_sparse_equals_live_row_oracle_order(cuda):
                            bits16_np(lay[5]), F=c["F"], FS=c["FS"], D=c["D"], topk=c["topk"])
     assert rel_err(f32_np(y), yc) < TOL
     _ = bf16_bits_to_f32
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B", [1, 3, 8, 130])
+@pytest.mark.parametrize("z", [0.02, 0.5, 0.9])
+def test_dense_form_is_bit_identical(cuda, B, z):
+    """The dense form (every row read) and the sparse form (zero rows skipped) run the same
+    reduction order, so their outputs are equal bit for bit, at any zero fraction -- the
+    property behind greedy-token identity of sparse and dense decoding."""
+    c = synth.decode_case(seed=500 + B, B=B, zero_frac=z, device=cuda)
+    lay = layouts(c)
+    for od in (torch.float32, torch.bfloat16):
+        ys = run(c, lay, out_dtype=od)
+        yd = run(c, lay, out_dtype=od, all_rows=True)
+        assert torch.equal(ys, yd)
+    assert rel_err(f32_np(yd.float()), oracle_y(c)) < 1e-2
+    assert hsd_b200.device_status() == 0
+
+
+@pytest.mark.gpu
+def test_verify_rows_equal_single_tokens(cuda):
+    """A token's output does not depend on the other rows of its launch up to 4 rows (the
+    verify steps of MTP-1..3): rows of a B = 3 launch equal B = 1 launches bit for bit."""
+    c = synth.decode_case(seed=77, B=3, zero_frac=0.9, device=cuda)
+    lay = layouts(c)
+    y3 = run(c, lay, out_dtype=torch.float32)
+    for b in range(3):
+        y1 = hsd_b200.sparse_down(c["h"][b:b + 1], c["sel"][b:b + 1], c["gains"][b:b + 1], *lay, F=c["F"],
+                                  FS=c["FS"], D=c["D"], topk=c["topk"], out_dtype=torch.float32)
+        assert torch.equal(y1[0], y3[b])

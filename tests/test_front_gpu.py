@@ -138,3 +138,52 @@ def test_qlinear_vs_oracle(cuda, B, in_f, out_f):
     resid = torch.randn((B, out_f), generator=gen, device=cuda).to(torch.bfloat16)
     y16 = qlinear(x, w, s, b, resid=resid)
     assert rel_err(f32_np(y16), f32_np(resid) + ref) < TOL16
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,D", [(1, 2688), (3, 2688), (5, 384)])
+def test_rms_norm_vs_torch(cuda, B, D):
+    from hsd_b200 import mamba as hm
+    from hsd_b200.rowops import rms_norm
+    gen = torch.Generator(device=cuda).manual_seed(B * D)
+    x = (torch.randn((B, D + 16), generator=gen, device=cuda) * 3).to(torch.bfloat16)[:, 8:8 + D]
+    w = (1 + 0.1 * torch.randn(D, generator=gen, device=cuda)).to(torch.bfloat16)
+    ref = hm.rms_norm(x, w, 1e-5)
+    y = rms_norm(x, w, 1e-5)
+    assert rel_err(f32_np(y), f32_np(ref)) < TOL16
+
+
+@pytest.mark.gpu
+def test_gated_rms_norm_vs_torch(cuda):
+    from hsd_b200 import mamba as hm
+    from hsd_b200.rowops import gated_rms_norm
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    B, I, G = 3, 4096, 8
+    y = torch.randn((B, I), generator=gen, device=cuda)
+    proj = torch.randn((B, I + 100), generator=gen, device=cuda).to(torch.bfloat16)
+    gate = proj[:, :I]
+    w = (1 + 0.1 * torch.randn(I, generator=gen, device=cuda)).to(torch.bfloat16)
+    ref = hm.gated_rms_norm(y, gate, w, I // G, 1e-5, torch.bfloat16)
+    out = gated_rms_norm(y, gate, w, I // G, 1e-5, torch.bfloat16)
+    assert rel_err(f32_np(out), f32_np(ref)) < TOL16
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,E,topk", [(1, 128, 6), (3, 128, 6), (4, 16, 4)])
+def test_router_vs_torch(cuda, B, E, topk):
+    from hsd_b200.rowops import Router
+    gen = torch.Generator(device=cuda).manual_seed(E + B)
+    D = 2688
+    R = torch.randn((E, D), generator=gen, device=cuda) * 0.02
+    x = torch.randn((B, D), generator=gen, device=cuda).to(torch.bfloat16)
+    router = Router(R, topk)
+    for _ in range(2):                                   # the ticket resets between calls
+        sel, gains = router(x)
+        sc = torch.sigmoid(x.float() @ R.t())
+        top, ref_sel = torch.topk(sc, topk, dim=-1)
+        assert torch.equal(torch.sort(sel.long(), -1).values, torch.sort(ref_sel, -1).values)
+        ref_g = top / top.sum(-1, keepdim=True)
+        order = torch.argsort(sel.long(), -1)
+        ref_order = torch.argsort(ref_sel, -1)
+        assert torch.allclose(gains[:, :topk].gather(1, order), ref_g.gather(1, ref_order), rtol=1e-5, atol=1e-6)
+        assert torch.all(gains[:, topk] == 1.0)
