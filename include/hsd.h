@@ -280,6 +280,20 @@ int hsd_router_topk(const void* x, int x_dtype, int64_t x_stride, const float* R
                     int topk, float* scores, unsigned int* ticket, int32_t* sel, float* gains,
                     void* stream);
 
+/* The attention of decode rows over a fixed-size cache (the reference model's GQA block at
+ * decode, mlx-lm nemotron_h, no positional encoding), for steps replayed from a captured
+ * graph: the position is read on the device. q [L, QH*HD] bf16 (row stride q_stride,
+ * a multiple of 8), kc / vc [KVH, max_len, HD] bf16 with rows pos .. pos+L-1 already
+ * written, *pos (device int64) the tokens before row 0; row l attends keys 0 .. pos+l with
+ * scale `scale` -> out [L, QH*HD] bf16. ws: fp32 workspace of
+ * hsd_attn_decode_workspace_bytes(L, QH, max_len) bytes. HD 64 or 128, QH/KVH <= 16. A row's
+ * result does not depend on the other rows of the call. pos + L > max_len is clamped and
+ * recorded as HSD_ERR_INDEX in the status word. */
+int hsd_attn_decode_workspace_bytes(int L, int QH, int max_len, size_t* bytes);
+int hsd_attn_decode(const void* q, int64_t q_stride, const void* kc, const void* vc,
+                    const int64_t* pos, void* out, float* ws, int L, int QH, int KVH, int HD,
+                    int max_len, float scale, void* stream);
+
 /* ---- allocation-free prefill ------------------------------------------------------ */
 
 /* No counterpart in the reference. For callers that cannot call cudaMalloc (code running

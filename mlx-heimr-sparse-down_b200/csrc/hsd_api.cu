@@ -26,6 +26,7 @@ int hsd_read_status_gemm(int* out, cudaStream_t st);
 int hsd_read_status_up(int* out, cudaStream_t st);
 int hsd_read_status_mamba(int* out, cudaStream_t st);
 int hsd_read_status_norm(int* out, cudaStream_t st);
+int hsd_read_status_attn(int* out, cudaStream_t st);
 
 extern "C" const char* hsd_last_error_string(void) { return hsd::g_last_error; }
 
@@ -37,7 +38,8 @@ extern "C" int hsd_device_status(int* status_out, void* stream) {
   int first = HSD_OK;
   int (*readers[])(int*, cudaStream_t) = {hsd_read_status_decode, hsd_read_status_prefill,
                                                 hsd_read_status_gemm, hsd_read_status_up,
-                                                hsd_read_status_mamba, hsd_read_status_norm};
+                                                hsd_read_status_mamba, hsd_read_status_norm,
+                                                hsd_read_status_attn};
   for (auto rd : readers) {
     int v = HSD_OK;
     int rc = rd(&v, st);

@@ -9,7 +9,7 @@
 //   router_topk     the MoE router of hsd/model.py:115 (mix.gate): logits = x . R_e in fp32,
 //                   scores = sigmoid(logits), the top-k experts by score (ties -> lower id),
 //                   gains = scores / sum(top-k scores), and gain 1 for the shared expert.
-//                   One warp per expert over all blocks; the last block to finish (a ticket
+//                   One block per (expert, row); the last block to finish (a ticket
 //                   counter in caller memory, taken with one atomic, no waiting) selects the
 //                   top k and resets the ticket for the next call.
 //
@@ -77,6 +77,50 @@ __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const void* x, int x
   }
 }
 
+// bf16 rows, D % 8 == 0, 16-byte aligned: each thread keeps its NV 8-value pieces in
+// registers, so the row is read once (the same arithmetic as rms_norm_kernel).
+template <int NV>
+__global__ void __launch_bounds__(kThreads) rms_norm_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
+                                                                  const __nv_bfloat16* __restrict__ w,
+                                                                  __nv_bfloat16* __restrict__ y, int D, float eps) {
+  __shared__ float red[kThreads / 32];
+  const int64_t r = blockIdx.x;
+  const int nq = D / 8;
+  uint4 xv[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int q = threadIdx.x + k * kThreads;
+    xv[k] = q < nq ? __ldg(reinterpret_cast<const uint4*>(x + r * x_stride) + q) : make_uint4(0, 0, 0, 0);
+    const uint32_t wd[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = __uint_as_float(wd[i] << 16), b = __uint_as_float(wd[i] & 0xffff0000u);
+      ss = fmaf(a, a, ss);
+      ss = fmaf(b, b, ss);
+    }
+  }
+  const float rs = rsqrtf(block_sum(ss, red) / D + eps);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int q = threadIdx.x + k * kThreads;
+    if (q >= nq) continue;
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w) + q);
+    const uint32_t xd[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+    const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t od[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float n0 = round_to(__uint_as_float(xd[i] << 16) * rs, HSD_BF16);
+      const float n1 = round_to(__uint_as_float(xd[i] & 0xffff0000u) * rs, HSD_BF16);
+      const __nv_bfloat16 o0 = __float2bfloat16_rn(__uint_as_float(wd[i] << 16) * n0);
+      const __nv_bfloat16 o1 = __float2bfloat16_rn(__uint_as_float(wd[i] & 0xffff0000u) * n1);
+      od[i] = static_cast<uint32_t>(__bfloat16_as_ushort(o0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(o1)) << 16);
+    }
+    reinterpret_cast<uint4*>(y + r * D)[q] = make_uint4(od[0], od[1], od[2], od[3]);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) gated_rms_norm_kernel(const void* yv, int y_dtype, int64_t y_stride,
                                                                    const void* gate, int g_dtype, int64_t g_stride,
                                                                    const void* w, int w_dtype, void* out,
@@ -102,27 +146,44 @@ __global__ void __launch_bounds__(kThreads) gated_rms_norm_kernel(const void* yv
 }
 
 // ---- router: logits, sigmoid, top-k, normalised gains ------------------------------
-constexpr int kRouterWarps = 8;          // experts per block
+constexpr int kRouterThreads = 128;      // one block per (expert, row)
+constexpr int kRouterWarps = kRouterThreads / 32;
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopk = 16;
 
-__global__ void __launch_bounds__(kRouterWarps * 32) router_topk_kernel(const void* x, int x_dtype, int64_t x_stride,
-                                                                         const float* __restrict__ R, int B, int D,
-                                                                         int E, int topk, float* scores,
-                                                                         unsigned int* ticket, int32_t* sel,
-                                                                         float* gains) {
-  // grid: (ceil(E / kRouterWarps), B); scores [B, E] fp32 scratch
+__global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(const void* x, int x_dtype, int64_t x_stride,
+                                                                      const float* __restrict__ R, int B, int D,
+                                                                      int E, int topk, float* scores,
+                                                                      unsigned int* ticket, int32_t* sel,
+                                                                      float* gains) {
+  // grid: (E, B); scores [B, E] fp32 scratch
+  __shared__ float red[kRouterWarps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int b = blockIdx.y;
-  const int e = blockIdx.x * kRouterWarps + warp;
-  if (e < E) {
+  const int e = blockIdx.x, b = blockIdx.y;
+  {
     const float* re = R + static_cast<int64_t>(e) * D;
     const int64_t xo = static_cast<int64_t>(b) * x_stride;
     float acc = 0.f;
-    for (int i = lane; i < D; i += 32) acc = fmaf(load_any(x, x_dtype, xo + i), re[i], acc);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) scores[static_cast<int64_t>(b) * E + e] = 1.f / (1.f + expf(-acc));
+    const bool vec = x_dtype == HSD_BF16 && D % 4 == 0 &&
+                     (reinterpret_cast<uintptr_t>(static_cast<const uint16_t*>(x) + xo) % 8) == 0 &&
+                     (reinterpret_cast<uintptr_t>(re) % 16) == 0;
+    if (vec) {                           // 4 weights (16 bytes) and 4 bf16 inputs (8 bytes) a load
+      const float4* r4 = reinterpret_cast<const float4*>(re);
+      const uint2* x4 = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + xo);
+#pragma unroll 4
+      for (int c = threadIdx.x; c < D / 4; c += kRouterThreads) {
+        const float4 rv = __ldg(r4 + c);
+        const uint2 xv = __ldg(x4 + c);
+        acc = fmaf(__uint_as_float(xv.x << 16), rv.x, acc);
+        acc = fmaf(__uint_as_float(xv.x & 0xffff0000u), rv.y, acc);
+        acc = fmaf(__uint_as_float(xv.y << 16), rv.z, acc);
+        acc = fmaf(__uint_as_float(xv.y & 0xffff0000u), rv.w, acc);
+      }
+    } else {
+      for (int i = threadIdx.x; i < D; i += kRouterThreads) acc = fmaf(load_any(x, x_dtype, xo + i), re[i], acc);
+    }
+    const float t = block_sum(acc, red);
+    if (threadIdx.x == 0) scores[static_cast<int64_t>(b) * E + e] = 1.f / (1.f + expf(-t));
   }
   // the last block of the whole grid selects the top k of every row
   __shared__ bool last;
@@ -136,20 +197,25 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_topk_kernel(const vo
   if (!last) return;
   __threadfence();
   if (threadIdx.x == 0) *ticket = 0u;
-  // one warp per row: k rounds of a warp arg-max over the row's scores (ties -> lower id)
+  // one warp per row: the row's scores into registers once (E <= 1024: 32 per lane), then
+  // k rounds of a warp arg-max over them (ties -> lower id)
+  constexpr int kPer = kMaxExperts / 32;
   for (int row = warp; row < B; row += kRouterWarps) {
     const volatile float* sc = scores + static_cast<int64_t>(row) * E;
-    float chosen_val[kMaxTopk];
-    int chosen_id[kMaxTopk];
-    float total = 0.f;
+    float v[kPer];
+#pragma unroll
+    for (int t = 0; t < kPer; ++t) {
+      const int i = lane + 32 * t;
+      v[t] = i < E ? sc[i] : -INFINITY;
+    }
+    float total = 0.f, chosen = 0.f;
     for (int k = 0; k < topk; ++k) {
-      float bv = -1.f;
+      float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int i = lane; i < E; i += 32) {
-        bool taken = false;
-        for (int j = 0; j < k; ++j) taken |= (chosen_id[j] == i);
-        const float v = sc[i];
-        if (!taken && (v > bv || (v == bv && i < bi))) { bv = v; bi = i; }
+#pragma unroll
+      for (int t = 0; t < kPer; ++t) {
+        const int i = lane + 32 * t;
+        if (v[t] > bv || (v[t] == bv && i < bi)) { bv = v[t]; bi = i; }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -157,17 +223,16 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_topk_kernel(const vo
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
         if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
       }
-      chosen_val[k] = bv;
-      chosen_id[k] = bi;
+      // the owner lane retires the chosen entry; lane k keeps the k-th choice
+#pragma unroll
+      for (int t = 0; t < kPer; ++t)
+        if (lane + 32 * t == bi) v[t] = -INFINITY;
+      if (lane == k) chosen = bv;
+      if (lane == 0) sel[static_cast<int64_t>(row) * topk + k] = bi;
       total += bv;
     }
-    if (lane == 0) {
-      for (int k = 0; k < topk; ++k) {
-        sel[static_cast<int64_t>(row) * topk + k] = chosen_id[k];
-        gains[static_cast<int64_t>(row) * (topk + 1) + k] = chosen_val[k] / (total + 1e-20f);
-      }
-      gains[static_cast<int64_t>(row) * (topk + 1) + topk] = 1.f;
-    }
+    if (lane < topk) gains[static_cast<int64_t>(row) * (topk + 1) + lane] = chosen / (total + 1e-20f);
+    if (lane == 0) gains[static_cast<int64_t>(row) * (topk + 1) + topk] = 1.f;
   }
 }
 
@@ -182,7 +247,22 @@ extern "C" int hsd_rms_norm(const void* x, int x_dtype, int64_t x_stride, const 
   if (!x || !w || !y || x_stride < D) return hsd::set_error(HSD_ERR_ARG, "hsd_rms_norm: null pointer or x_stride < D");
   if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype) || !dtype_ok(y_dtype))
     return hsd::set_error(HSD_ERR_DTYPE, "hsd_rms_norm: dtype codes %d %d %d", x_dtype, w_dtype, y_dtype);
-  rms_norm_kernel<<<B, kThreads, 0, hsd::as_stream(stream)>>>(x, x_dtype, x_stride, w, w_dtype, y, y_dtype, D, eps);
+  cudaStream_t st = hsd::as_stream(stream);
+  const int nv = (D / 8 + kThreads - 1) / kThreads;
+  if (x_dtype == HSD_BF16 && w_dtype == HSD_BF16 && y_dtype == HSD_BF16 && D % 8 == 0 && nv <= 4 &&
+      x_stride % 8 == 0 && hsd::aligned(x, 16) && hsd::aligned(w, 16) && hsd::aligned(y, 16)) {
+    const auto* xb = static_cast<const __nv_bfloat16*>(x);
+    const auto* wb = static_cast<const __nv_bfloat16*>(w);
+    auto* yb = static_cast<__nv_bfloat16*>(y);
+    switch (nv) {
+      case 1: rms_norm_bf16_kernel<1><<<B, kThreads, 0, st>>>(xb, x_stride, wb, yb, D, eps); break;
+      case 2: rms_norm_bf16_kernel<2><<<B, kThreads, 0, st>>>(xb, x_stride, wb, yb, D, eps); break;
+      case 3: rms_norm_bf16_kernel<3><<<B, kThreads, 0, st>>>(xb, x_stride, wb, yb, D, eps); break;
+      default: rms_norm_bf16_kernel<4><<<B, kThreads, 0, st>>>(xb, x_stride, wb, yb, D, eps); break;
+    }
+  } else {
+    rms_norm_kernel<<<B, kThreads, 0, st>>>(x, x_dtype, x_stride, w, w_dtype, y, y_dtype, D, eps);
+  }
   return hsd::check_launch("hsd_rms_norm");
 }
 
@@ -213,8 +293,8 @@ extern "C" int hsd_router_topk(const void* x, int x_dtype, int64_t x_stride, con
   if (!x || !R || !scores || !ticket || !sel || !gains || x_stride < D)
     return hsd::set_error(HSD_ERR_ARG, "hsd_router_topk: null pointer or x_stride < D");
   if (!dtype_ok(x_dtype)) return hsd::set_error(HSD_ERR_DTYPE, "hsd_router_topk: x dtype code %d", x_dtype);
-  dim3 grid((E + kRouterWarps - 1) / kRouterWarps, B);
-  router_topk_kernel<<<grid, kRouterWarps * 32, 0, hsd::as_stream(stream)>>>(x, x_dtype, x_stride, R, B, D, E, topk,
-                                                                             scores, ticket, sel, gains);
+  dim3 grid(E, B);
+  router_topk_kernel<<<grid, kRouterThreads, 0, hsd::as_stream(stream)>>>(x, x_dtype, x_stride, R, B, D, E, topk,
+                                                                          scores, ticket, sel, gains);
   return hsd::check_launch("hsd_router_topk");
 }

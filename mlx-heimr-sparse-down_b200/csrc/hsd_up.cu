@@ -12,10 +12,10 @@
 //          rows [B, topk+1, D] are summed in slot order (+ resid) by the prefill path's
 //          reduce kernel, so the dense output is deterministic.
 //
-// Work split: one block per (token b, part, tile of 32 output rows), part k < topk the
+// Work split: one block per (token b, part, tile of 16 output rows), part k < topk the
 // routed expert sel[b, k] and part topk the shared expert; a flat grid of
-// B * (topk * tiles(routed) + tiles(shared)) blocks (464 for one token of the reference
-// shapes in the up form, 588 in the dense form).
+// B * (topk * tiles(routed) + tiles(shared)) blocks of 16 rows (928 for one token of the
+// reference shapes in the up form, 1176 in the dense form).
 // Each warp owns 4 rows. Lane l reads the 16-byte pieces l, l+32, l+64, .. of a row (a
 // piece = 32 consecutive columns = half a 64-group), so every row is read by one coalesced
 // sweep and each weight byte once. All 4 rows' pieces are loaded before any arithmetic, for
@@ -36,10 +36,10 @@ HSD_DEFINE_STATUS(up)
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRowsPerWarp = 4;
-constexpr int kRowsPerBlock = kWarps * kRowsPerWarp;   // 32
+constexpr int kRowsPerBlock = kWarps * kRowsPerWarp;   // 16
 constexpr int kPad = 36;                                // floats per 32-column piece in smem
 constexpr int kMaxD = 8192;                             // longest reduction (8 pieces a lane)
 
@@ -70,6 +70,31 @@ __device__ __forceinline__ float load_x(const void* x, int dtype, int64_t i) {
     case HSD_F32: return reinterpret_cast<const float*>(x)[i];
     case HSD_F16: return __half2float(reinterpret_cast<const __half*>(x)[i]);
     default: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
+  }
+}
+
+// 8 consecutive values x[i .. i+7] as fp32; vec: the address is 16-byte aligned
+__device__ __forceinline__ void load8(const void* x, int dtype, int64_t i, bool vec, float* v) {
+  if (vec && dtype != HSD_F32) {
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + i));
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (dtype == HSD_BF16) {
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+      } else {
+        v[2 * k] = __half2float(__ushort_as_half(static_cast<uint16_t>(w[k] & 0xffffu)));
+        v[2 * k + 1] = __half2float(__ushort_as_half(static_cast<uint16_t>(w[k] >> 16)));
+      }
+    }
+  } else if (vec) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(x) + i));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(x) + i) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = load_x(x, dtype, i + k);
   }
 }
 
@@ -157,8 +182,10 @@ __global__ void __launch_bounds__(kThreads) moe_qgemv_kernel(const UpParams p, i
     return;
   }
 
-  // issue this warp's weight loads first: they do not depend on the token
+  // issue this warp's weight, scale and bias loads first: they do not depend on the token,
+  // and none of them may wait behind another (each is a DRAM round trip)
   uint4 wv[kRowsPerWarp][MAXC];
+  uint16_t sv[kRowsPerWarp][MAXC], bv[kRowsPerWarp][MAXC];
 #pragma unroll
   for (int r = 0; r < kRowsPerWarp; ++r) {
     const int row = min(r0 + r, rows - 1);
@@ -169,24 +196,47 @@ __global__ void __launch_bounds__(kThreads) moe_qgemv_kernel(const UpParams p, i
       wv[r][c] = pc < NP ? hsd::ldg_nc_v4(wr + 4 * pc) : make_uint4(0, 0, 0, 0);
     }
   }
-
-  // the input row, as padded 32-float pieces, and the sum of every piece
-  const int64_t xb = static_cast<int64_t>(bi) * p.x_stride + (MODE != kDense ? 0 : static_cast<int64_t>(part) * p.F);
-  for (int i = tid; i < red; i += kThreads) xs[(i >> 5) * kPad + (i & 31)] = load_x(p.x, p.x_dtype, xb + i);
-  __syncthreads();
-  for (int pc = tid; pc < NP; pc += kThreads) {
-    float s = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < 32; ++j) s += xs[pc * kPad + j];
-    xsum[pc] = s;
-  }
-  __syncthreads();
-
 #pragma unroll
   for (int r = 0; r < kRowsPerWarp; ++r) {
     const int row = min(r0 + r, rows - 1);
     const uint16_t* sr = S + static_cast<int64_t>(row) * GR;
     const uint16_t* br = Bz + static_cast<int64_t>(row) * GR;
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      const int pc = lane + 32 * c;
+      sv[r][c] = pc < NP ? __ldg(sr + (pc >> 1)) : static_cast<uint16_t>(0);
+      bv[r][c] = pc < NP ? __ldg(br + (pc >> 1)) : static_cast<uint16_t>(0);
+    }
+  }
+
+  // the input row, as padded 32-float pieces, and the sum of every piece: a thread loads a
+  // quarter piece (8 values, one 16-byte load when the row is aligned), 4 adjacent lanes
+  // sum a piece with two shuffles
+  const int64_t xb = static_cast<int64_t>(bi) * p.x_stride + (MODE != kDense ? 0 : static_cast<int64_t>(part) * p.F);
+  const int esz = p.x_dtype == HSD_F32 ? 4 : 2;
+  const bool vec = (reinterpret_cast<uintptr_t>(p.x) + static_cast<uintptr_t>(xb) * esz) % 16 == 0;
+  const int nq = red / 8;
+  for (int q0 = 0; q0 < nq; q0 += kThreads) {
+    const int q = q0 + tid;
+    float v[8];
+    if (q < nq) load8(p.x, p.x_dtype, xb + 8 * q, vec, v);
+    else
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    float sq = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+    sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+    if (q < nq) {
+      float4* dst = reinterpret_cast<float4*>(xs + (q >> 2) * kPad + (q & 3) * 8);
+      dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+      dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+      if ((q & 3) == 0) xsum[q >> 2] = sq;
+    }
+  }
+  __syncthreads();
+
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) {
     float acc = 0.f;
 #pragma unroll
     for (int c = 0; c < MAXC; ++c) {
@@ -199,8 +249,8 @@ __global__ void __launch_bounds__(kThreads) moe_qgemv_kernel(const UpParams p, i
         d = word_dot(wv[r][c].z, xv[4], xv[5], d);
         d = word_dot(wv[r][c].w, xv[6], xv[7], d);
         const float sx = xsum[pc];
-        const float sc = hsd::bits16_to_f32<ST>(sr[pc >> 1]);
-        const float bc = hsd::bits16_to_f32<ST>(br[pc >> 1]);
+        const float sc = hsd::bits16_to_f32<ST>(sv[r][c]);
+        const float bc = hsd::bits16_to_f32<ST>(bv[r][c]);
         acc = fmaf(sc * 16.f, d - sx, fmaf(bc, sx, acc));
       }
     }

@@ -53,6 +53,8 @@ SIGNATURES = {
     "hsd_rms_norm": [_P, _I, _L, _P, _I, _P, _I, _I, _I, ctypes.c_float, _P],
     "hsd_gated_rms_norm": [_P, _I, _L, _P, _I, _L, _P, _I, _P, _I, _I, _I, _I, ctypes.c_float, _P],
     "hsd_router_topk": [_P, _I, _L, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P],
+    "hsd_attn_decode_workspace_bytes": [_I, _I, _I, _P],
+    "hsd_attn_decode": [_P, _L, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _P],
     "hsd_dense_down_decode": [_P, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I,
                               _I, _P],
     "hsd_prefill_noalloc_max_bytes": [_P],

@@ -39,7 +39,7 @@ from .decode import dense_down, sparse_down
 from .front import moe_up, qlinear
 from .layout import to_neuron_major
 from .prefill import sparse_down_prefill
-from .rowops import Router, gated_rms_norm, rms_norm
+from .rowops import DecodeAttention, Router, gated_rms_norm, rms_norm
 
 MODES = ("dense", "sparse", "stock")
 QGEMV_ROWS = 8          # rows up to which the linears use the 4-bit matrix-vector kernel
@@ -215,6 +215,7 @@ class AttnBlock:
         self.wqkv = QLinear((a.q_heads + 2 * a.kv_heads) * a.head_dim, D, gen, device, a.std)
         self.wo = QLinear(D, a.q_heads * a.head_dim, gen, device, a.std)
         self.keys = torch.arange(a.max_len, device=device)
+        self.attn = DecodeAttention(a.q_heads, a.kv_heads, a.head_dim, a.max_len, QGEMV_ROWS, device)
 
     def rows(self, x, kv, pos):
         a = self.a
@@ -231,13 +232,10 @@ class AttnBlock:
         kv.v.index_copy_(1, pos + rows, v.transpose(0, 1))
         sdpa = torch.nn.functional.scaled_dot_product_attention
         if L <= QGEMV_ROWS:
-            # decode rows one at a time, each the same launch a single step makes, so a
-            # verify row equals the token decoded alone bit for bit
-            outs = []
-            for l in range(L):
-                mask = self.keys[None, :] <= (pos + l)[:, None]              # [1, max_len]
-                outs.append(sdpa(q[l].reshape(1, kvh, g, hd), kv.k[None], kv.v[None], attn_mask=mask[None, None]))
-            o = torch.cat(outs, 0).reshape(L, qh * hd)
+            # decode rows: hsd_attn_decode over the keys up to each row's position, a row's
+            # result independent of the launch's other rows (a verify row equals the token
+            # decoded alone bit for bit)
+            o = self.attn(qkv[:, :qh * hd], kv.k, kv.v, pos)
         else:
             # the g query heads of a KV head as g*L rows (row r = head j*L + l), one mask row each
             qg = q.permute(1, 2, 0, 3).reshape(1, kvh, g * L, hd)

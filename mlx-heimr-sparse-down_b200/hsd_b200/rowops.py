@@ -53,3 +53,27 @@ class Router:
                   self.D, self.E, self.topk, _lib.ptr(sc), _lib.ptr(self.ticket), _lib.ptr(sel), _lib.ptr(gains),
                   _lib.stream_of(x))
         return sel, gains
+
+
+class DecodeAttention:
+    """GQA attention of decode rows over a fixed-size cache with a device-side position
+    (hsd_attn_decode): q [L, QH*HD] (rows may be strided), k / v caches [KVH, max_len, HD]
+    bf16, pos int64 [1] on the device -> out [L, QH*HD] bf16. Keeps its fp32 workspace."""
+
+    def __init__(self, q_heads, kv_heads, head_dim, max_len, rows, device):
+        import ctypes
+        self.QH, self.KVH, self.HD, self.max_len, self.rows = q_heads, kv_heads, head_dim, max_len, rows
+        nb = ctypes.c_size_t(0)
+        _lib.call("hsd_attn_decode_workspace_bytes", rows, q_heads, max_len, ctypes.byref(nb))
+        self.ws = torch.empty(nb.value // 4, dtype=torch.float32, device=device)
+        self.scale = head_dim ** -0.5
+
+    def __call__(self, q, kc, vc, pos):
+        L = q.shape[0]
+        if L > self.rows or q.dtype != torch.bfloat16 or q.stride(1) != 1:
+            raise ValueError(f"DecodeAttention: at most {self.rows} bf16 rows with contiguous columns")
+        out = torch.empty((L, self.QH * self.HD), dtype=torch.bfloat16, device=q.device)
+        _lib.call("hsd_attn_decode", _lib.ptr(q), q.stride(0), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(pos),
+                  _lib.ptr(out), _lib.ptr(self.ws), L, self.QH, self.KVH, self.HD, self.max_len, float(self.scale),
+                  _lib.stream_of(q))
+        return out

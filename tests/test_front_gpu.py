@@ -187,3 +187,33 @@ def test_router_vs_torch(cuda, B, E, topk):
         ref_order = torch.argsort(ref_sel, -1)
         assert torch.allclose(gains[:, :topk].gather(1, order), ref_g.gather(1, ref_order), rtol=1e-5, atol=1e-6)
         assert torch.all(gains[:, topk] == 1.0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("L,pos,HD,QH,KVH", [(1, 0, 128, 32, 2), (3, 200, 128, 32, 2), (4, 1000, 64, 4, 2),
+                                             (1, 4095, 128, 32, 2), (2, 63, 128, 16, 1)])
+def test_decode_attention_vs_fp32_softmax(cuda, L, pos, HD, QH, KVH):
+    """hsd_attn_decode against an fp32 softmax(q K^T / sqrt(HD)) V over each row's keys, and
+    a row's result equals the same row computed alone (bit for bit)."""
+    from hsd_b200.rowops import DecodeAttention
+    max_len = 4096
+    gen = torch.Generator(device=cuda).manual_seed(L + pos + HD)
+    kc = torch.randn((KVH, max_len, HD), generator=gen, device=cuda).to(torch.bfloat16)
+    vc = torch.randn((KVH, max_len, HD), generator=gen, device=cuda).to(torch.bfloat16)
+    wide = torch.randn((L, QH * HD + 3 * 8 * HD), generator=gen, device=cuda).to(torch.bfloat16)
+    q = wide[:, :QH * HD]                                    # strided rows, as the qkv slice
+    p = torch.tensor([pos], dtype=torch.int64, device=cuda)
+    att = DecodeAttention(QH, KVH, HD, max_len, 8, cuda)
+    out = att(q, kc, vc, p)
+    g = QH // KVH
+    for l in range(L):
+        n = pos + l + 1
+        qf = q[l].float().view(QH, HD)
+        kf = kc[:, :n].float().repeat_interleave(g, 0)       # [QH, n, HD]
+        vf = vc[:, :n].float().repeat_interleave(g, 0)
+        w = torch.softmax(torch.einsum("hd,hnd->hn", qf, kf) / HD ** 0.5, -1)
+        ref = torch.einsum("hn,hnd->hd", w, vf).reshape(-1)
+        assert rel_err(f32_np(out[l]), f32_np(ref)) < TOL16
+        alone = att(q[l:l + 1], kc, vc, p + l)
+        assert torch.equal(alone[0], out[l])
+    assert hsd_b200.device_status() == 0
