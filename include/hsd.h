@@ -222,8 +222,10 @@ int hsd_mamba_ssm_step(const void* xbc, int x_dtype, int64_t xbc_stride, const v
  *   h[b, topk*F + f] = relu(sum_d Wsu[f, d] * x[b, d])^2             for f < FS
  * Up weights in the checkpoint layout along the hidden axis: uw [E, F, D/8] u32, us / ub
  * [E, F, D/64] (s_dtype); suw [FS, D/8], sus / sub [FS, D/64]. x [B, D] with row stride
- * x_stride elements; h [B, topk*F + FS] contiguous. fp32 accumulation, one rounding to
- * h_dtype. D % 64 == 0, D <= 8192, uw / suw 16-byte aligned; topk == 0 (shared only) and
+ * x_stride elements; h [B, topk*F + FS] contiguous. On the tensor cores (mma.m16n8k16): x
+ * rounded to fp16 (exact for bf16 inside fp16's range), the nibbles as exact fp16 integers,
+ * fp32 accumulation, one rounding to h_dtype; a token's outputs do not depend on the other
+ * tokens of the call. D % 64 == 0, D <= 8192, uw / suw 16-byte aligned; topk == 0 (shared only) and
  * FS == 0 (routed only) are allowed. An expert id outside [0, E) gives zeros for that slot
  * and HSD_ERR_INDEX in the status word. */
 int hsd_moe_up_decode(const void* x, int x_dtype, int64_t x_stride, const int32_t* sel,
@@ -246,11 +248,14 @@ int hsd_dense_down_decode(const void* h, int h_dtype, const int32_t* sel, const 
                           int E, void* stream);
 
 /* The model's other 4-bit linears at decode (mlx QuantizedLinear, the layers around the hot
- * path: Mamba in / out projections, attention projections, lm_head), same kernel:
+ * path: Mamba in / out projections, attention projections, lm_head), on the tensor cores as
+ * hsd_moe_up_decode (the weights read once for up to 8 rows, a row's result independent of
+ * the other rows):
  *   y[b, o] = (resid[b, o] +) sum_i W[o, i] * x[b, i]
  * w [out_f, in_f/8] u32, s / b [out_f, in_f/64] (s_dtype); x [B, in_f] with row stride
- * x_stride; resid (may be NULL) and y [B, out_f] contiguous in y_dtype. fp32 accumulation,
- * the residual added in fp32, one rounding. in_f % 64 == 0, in_f <= 8192, w 16-byte aligned. */
+ * x_stride; resid (may be NULL) and y [B, out_f] contiguous in y_dtype. x in fp16, fp32
+ * accumulation, the residual added in fp32, one rounding. in_f % 64 == 0, in_f <= 8192, w
+ * 16-byte aligned. */
 int hsd_qlinear_decode(const void* x, int x_dtype, int64_t x_stride, const uint32_t* w, const void* s,
                        const void* b, int s_dtype, const void* resid, void* y, int y_dtype, int B,
                        int in_f, int out_f, void* stream);

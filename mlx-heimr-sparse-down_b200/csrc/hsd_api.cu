@@ -27,6 +27,7 @@ int hsd_read_status_up(int* out, cudaStream_t st);
 int hsd_read_status_mamba(int* out, cudaStream_t st);
 int hsd_read_status_norm(int* out, cudaStream_t st);
 int hsd_read_status_attn(int* out, cudaStream_t st);
+int hsd_read_status_qmma(int* out, cudaStream_t st);
 
 extern "C" const char* hsd_last_error_string(void) { return hsd::g_last_error; }
 
@@ -39,7 +40,7 @@ extern "C" int hsd_device_status(int* status_out, void* stream) {
   int (*readers[])(int*, cudaStream_t) = {hsd_read_status_decode, hsd_read_status_prefill,
                                                 hsd_read_status_gemm, hsd_read_status_up,
                                                 hsd_read_status_mamba, hsd_read_status_norm,
-                                                hsd_read_status_attn};
+                                                hsd_read_status_attn, hsd_read_status_qmma};
   for (auto rd : readers) {
     int v = HSD_OK;
     int rc = rd(&v, st);

@@ -31,10 +31,22 @@ HSD_DEFINE_STATUS(gemm)
 
 namespace {
 
-constexpr int BM = 128, BN = 192, BK = 64;
-constexpr int STAGES = 7;                                     // A / packed-W / scale stages in flight
-constexpr int BSTAGES = 2;                                    // dequantised B buffers
-constexpr int DQ_WARPS = 12;
+#ifndef HSD_GEMM_BN
+#define HSD_GEMM_BN 192
+#endif
+constexpr int BM = 128, BN = HSD_GEMM_BN, BK = 64;
+#ifndef HSD_GEMM_STAGES
+#define HSD_GEMM_STAGES 7
+#endif
+#ifndef HSD_GEMM_BSTAGES
+#define HSD_GEMM_BSTAGES 2
+#endif
+constexpr int STAGES = HSD_GEMM_STAGES;                       // A / packed-W / scale stages in flight
+constexpr int BSTAGES = HSD_GEMM_BSTAGES;                     // dequantised B buffers
+#ifndef HSD_GEMM_DQ_WARPS
+#define HSD_GEMM_DQ_WARPS 12
+#endif
+constexpr int DQ_WARPS = HSD_GEMM_DQ_WARPS;
 constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_EPI0 = 2, WARP_CONV = 6, WARP_DQ0 = 7;
 constexpr int NWARPS = WARP_DQ0 + DQ_WARPS, THREADS = NWARPS * 32;
 constexpr int DQ_THREADS = DQ_WARPS * 32;
@@ -369,13 +381,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t* sbh = reinterpret_cast<uint32_t*>(gbase + OFF_SBH + stage * SB_BYTES);
         for (int t = lane; t < 2 * WPB; t += 32) {          // t < 24: scales of word t, else biases
           const int wd = t % WPB, which = t / WPB;
-          const uint32_t* src = sb + which * (BN / 2) + wd * 4;   // 8 values of word wd: (0,1)(2,3)(4,5)(6,7)
-          uint32_t* dst = sbh + which * (BN / 2) + wd * 4;          // pairs (0,4)(1,5)(2,6)(3,7)
-          const uint32_t a = src[0], b = src[1], c = src[2], dd = src[3];
-          dst[0] = pair_to_h2<ST>(__byte_perm(a, c, 0x5410));
-          dst[1] = pair_to_h2<ST>(__byte_perm(a, c, 0x7632));
-          dst[2] = pair_to_h2<ST>(__byte_perm(b, dd, 0x5410));
-          dst[3] = pair_to_h2<ST>(__byte_perm(b, dd, 0x7632));
+          // 8 values of word wd: (0,1)(2,3)(4,5)(6,7) -> pairs (0,4)(1,5)(2,6)(3,7), one 16-byte
+          // load and store per lane (consecutive lanes, consecutive 16-byte chunks)
+          const uint4 v = *reinterpret_cast<const uint4*>(sb + which * (BN / 2) + wd * 4);
+          *reinterpret_cast<uint4*>(sbh + which * (BN / 2) + wd * 4) =
+              make_uint4(pair_to_h2<ST>(__byte_perm(v.x, v.z, 0x5410)), pair_to_h2<ST>(__byte_perm(v.x, v.z, 0x7632)),
+                         pair_to_h2<ST>(__byte_perm(v.y, v.w, 0x5410)), pair_to_h2<ST>(__byte_perm(v.y, v.w, 0x7632)));
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_conv(stage));

@@ -1,44 +1,53 @@
 // 4-bit g64 matrix-vector products over the selected experts of decode rows, on the
-// checkpoint layout (rows = outputs, 4-bit groups of 64 along the reduction axis):
+// checkpoint layout (rows = outputs, 4-bit groups of 64 along the reduction axis). The C-ABI
+// entry points of this file:
 //
-//   up     the MoE front end's up projections with ReLU^2 (the reference's
-//          hsd/model.py:110-121: mlx gather_qmm of the normalised token against fc1 of each
-//          selected expert, the shared expert's quantised up_proj, relu2): uw [E, F, D/8],
-//          one x row per token shared by every part, output h [B, topk*F + FS].
-//   dense  the stock (dense) MoE down projection the sparse kernel is compared with
-//          (hsd/model.py:132-133 decode_dense, mlx gather_qmm of fc2 and the shared
-//          down_proj): w [E, D, F/8], part k reads its own slice h[b, k*F ..], every weight
-//          of the selected experts is read, the part's gain is applied and the fp32 partial
-//          rows [B, topk+1, D] are summed in slot order (+ resid) by the prefill path's
-//          reduce kernel, so the dense output is deterministic.
+//   hsd_moe_up_decode   the MoE front end's up projections with ReLU^2 (the reference's
+//                       hsd/model.py:110-121), and
+//   hsd_qlinear_decode  the model's plain 4-bit linears -- both computed on the tensor
+//                       cores by csrc/hsd_qmma.cu;
+//   hsd_dense_down_decode  the stock (dense) MoE down projection the sparse kernel is
+//          compared with (hsd/model.py:132-133 decode_dense, mlx gather_qmm of fc2 and the
+//          shared down_proj), by the fp32 CUDA-core kernel below: part k reads its own slice
+//          h[b, k*F ..], every weight of the selected experts is read, the part's gain is
+//          applied and the fp32 partial rows [B, topk+1, D] are summed in slot order (+ resid)
+//          by the prefill path's reduce kernel, so the dense output is deterministic.
 //
-// Work split: one block per (token b, part, tile of 16 output rows), part k < topk the
-// routed expert sel[b, k] and part topk the shared expert; a flat grid of
-// B * (topk * tiles(routed) + tiles(shared)) blocks of 16 rows (928 for one token of the
-// reference shapes in the up form, 1176 in the dense form).
-// Each warp owns 4 rows. Lane l reads the 16-byte pieces l, l+32, l+64, .. of a row (a
-// piece = 32 consecutive columns = half a 64-group), so every row is read by one coalesced
-// sweep and each weight byte once. All 4 rows' pieces are loaded before any arithmetic, for
-// memory-level parallelism.
+// The CUDA-core kernel: one block per (token b, part, tile of 16 output rows), part k < topk
+// the routed expert sel[b, k] and part topk the shared expert (1176 blocks for one token of
+// the reference shapes). Each warp owns one row (16 warps a block, so many warps are in
+// flight per SM to hide the memory latency). Lane l reads the 16-byte pieces l, l+32, l+64,
+// .. of a row (a piece = 32 consecutive columns = half a 64-group), so every row is read by
+// one coalesced sweep and each weight byte once; all of the row's pieces, scales and biases
+// are loaded before any arithmetic.
 //
 // Arithmetic per piece (q the nibble, x the token in fp32 shared memory):
 //   u = 1 + q/16 is built from the nibble by bit operations (exponent of 1.0 with q in the
 //   top mantissa bits), d = sum u*x, so sum q*x = 16 (d - sum x) with sum x of the piece
 //   precomputed once per block; the piece adds s * 16 (d - sx) + b * sx. fp32 throughout,
-//   a warp-shuffle sum per row, relu^2 and one rounding to the output type.
+//   a warp-shuffle sum per row and one rounding to the output type.
 //
 // The token lives in shared memory as pieces of 32 floats padded to 36, so the eight lanes
 // of each quarter-warp phase of a 128-bit shared load hit distinct banks.
 #include "hsd_common.cuh"
 #include "hsd_prefill.cuh"
 
+namespace hsd {
+// the tensor-core forms (csrc/hsd_qmma.cu) of the up and linear products
+int qmma_moe_up(const void* x, int x_dtype, int64_t x_stride, const int32_t* sel, const uint32_t* uw,
+                const void* us, const void* ub, int s_dtype, const uint32_t* suw, const void* sus, const void* sub,
+                void* h, int h_dtype, int B, int D, int F, int FS, int topk, int E, cudaStream_t st);
+int qmma_linear(const void* x, int x_dtype, int64_t x_stride, const uint32_t* w, const void* s, const void* b,
+                int s_dtype, const void* resid, void* y, int y_dtype, int B, int in_f, int out_f, cudaStream_t st);
+}  // namespace hsd
+
 HSD_DEFINE_STATUS(up)
 
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kRowsPerWarp = 4;
+constexpr int kRowsPerWarp = 1;                         // one row per warp: many warps in flight
 constexpr int kRowsPerBlock = kWarps * kRowsPerWarp;   // 16
 constexpr int kPad = 36;                                // floats per 32-column piece in smem
 constexpr int kMaxD = 8192;                             // longest reduction (8 pieces a lane)
@@ -235,25 +244,36 @@ __global__ void __launch_bounds__(kThreads) moe_qgemv_kernel(const UpParams p, i
   }
   __syncthreads();
 
+  // a piece of the token is read from shared memory once and applied to the warp's rows;
+  // each row still accumulates its pieces in ascending order
+  float accr[kRowsPerWarp];
 #pragma unroll
-  for (int r = 0; r < kRowsPerWarp; ++r) {
-    float acc = 0.f;
+  for (int r = 0; r < kRowsPerWarp; ++r) accr[r] = 0.f;
 #pragma unroll
-    for (int c = 0; c < MAXC; ++c) {
-      const int pc = lane + 32 * c;
-      if (pc < NP) {
-        const float4* xv = reinterpret_cast<const float4*>(xs + pc * kPad);
+  for (int c = 0; c < MAXC; ++c) {
+    const int pc = lane + 32 * c;
+    if (pc < NP) {
+      const float4* xp = reinterpret_cast<const float4*>(xs + pc * kPad);
+      float4 xv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[i] = xp[i];
+      const float sx = xsum[pc];
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) {
         float d = 0.f;
         d = word_dot(wv[r][c].x, xv[0], xv[1], d);
         d = word_dot(wv[r][c].y, xv[2], xv[3], d);
         d = word_dot(wv[r][c].z, xv[4], xv[5], d);
         d = word_dot(wv[r][c].w, xv[6], xv[7], d);
-        const float sx = xsum[pc];
         const float sc = hsd::bits16_to_f32<ST>(sv[r][c]);
         const float bc = hsd::bits16_to_f32<ST>(bv[r][c]);
-        acc = fmaf(sc * 16.f, d - sx, fmaf(bc, sx, acc));
+        accr[r] = fmaf(sc * 16.f, d - sx, fmaf(bc, sx, accr[r]));
       }
     }
+  }
+#pragma unroll
+  for (int r = 0; r < kRowsPerWarp; ++r) {
+    float acc = accr[r];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0 && r0 + r < rows) {
@@ -321,20 +341,8 @@ extern "C" int hsd_moe_up_decode(const void* x, int x_dtype, int64_t x_stride, c
     return hsd::set_error(HSD_ERR_ARG, "hsd_moe_up_decode: shared part needs suw, sus, sub");
   if ((topk > 0 && !hsd::aligned(uw, 16)) || (FS > 0 && !hsd::aligned(suw, 16)))
     return hsd::set_error(HSD_ERR_ALIGN, "hsd_moe_up_decode: packed weights must be 16-byte aligned");
-  UpParams p;
-  p.x = x; p.x_stride = x_stride; p.x_dtype = x_dtype; p.sel = sel; p.gains = nullptr; p.resid = nullptr;
-  p.uw = uw; p.us = static_cast<const uint16_t*>(us); p.ub = static_cast<const uint16_t*>(ub);
-  p.suw = suw; p.sus = static_cast<const uint16_t*>(sus); p.sub = static_cast<const uint16_t*>(sub);
-  p.h = h; p.h_dtype = h_dtype;
-  p.B = B; p.D = D; p.F = F; p.FS = FS; p.topk = topk; p.E = E;
-  p.tiles_routed = topk > 0 ? (F + kRowsPerBlock - 1) / kRowsPerBlock : 0;
-  p.tiles_shared = (FS + kRowsPerBlock - 1) / kRowsPerBlock;
-  p.tiles_per_b = topk * p.tiles_routed + p.tiles_shared;
-  const int64_t grid = static_cast<int64_t>(B) * p.tiles_per_b;
-  if (grid > 0x7fffffff) return hsd::set_error(HSD_ERR_SHAPE, "hsd_moe_up_decode: grid too large");
-  cudaStream_t st = hsd::as_stream(stream);
-  return s_dtype == HSD_BF16 ? launch_qgemv<kUp, __nv_bfloat16>(p, D, static_cast<int>(grid), st, "hsd_moe_up_decode")
-                             : launch_qgemv<kUp, __half>(p, D, static_cast<int>(grid), st, "hsd_moe_up_decode");
+  return hsd::qmma_moe_up(x, x_dtype, x_stride, sel, uw, us, ub, s_dtype, suw, sus, sub, h, h_dtype, B, D, F, FS,
+                          topk, E, hsd::as_stream(stream));
 }
 
 extern "C" int hsd_dense_down_decode(const void* h, int h_dtype, const int32_t* sel, const float* gains,
@@ -393,18 +401,6 @@ extern "C" int hsd_qlinear_decode(const void* x, int x_dtype, int64_t x_stride, 
   if (!x || !w || !s || !b || !y || x_stride < in_f)
     return hsd::set_error(HSD_ERR_ARG, "%s: null pointer or x_stride < in_f", who);
   if (!hsd::aligned(w, 16)) return hsd::set_error(HSD_ERR_ALIGN, "%s: packed weights must be 16-byte aligned", who);
-  UpParams p;
-  p.x = x; p.x_stride = x_stride; p.x_dtype = x_dtype; p.sel = nullptr; p.gains = nullptr; p.resid = resid;
-  p.uw = nullptr; p.us = nullptr; p.ub = nullptr;
-  p.suw = w; p.sus = static_cast<const uint16_t*>(s); p.sub = static_cast<const uint16_t*>(b);
-  p.h = y; p.h_dtype = y_dtype;
-  p.B = B; p.D = in_f; p.F = 0; p.FS = out_f; p.topk = 0; p.E = 0;
-  p.tiles_routed = 0;
-  p.tiles_shared = (out_f + kRowsPerBlock - 1) / kRowsPerBlock;
-  p.tiles_per_b = p.tiles_shared;
-  const int64_t grid = static_cast<int64_t>(B) * p.tiles_per_b;
-  if (grid > 0x7fffffff) return hsd::set_error(HSD_ERR_SHAPE, "%s: grid too large", who);
-  cudaStream_t st = hsd::as_stream(stream);
-  return s_dtype == HSD_BF16 ? launch_qgemv<kLinear, __nv_bfloat16>(p, in_f, static_cast<int>(grid), st, who)
-                             : launch_qgemv<kLinear, __half>(p, in_f, static_cast<int>(grid), st, who);
+  return hsd::qmma_linear(x, x_dtype, x_stride, w, s, b, s_dtype, resid, y, y_dtype, B, in_f, out_f,
+                          hsd::as_stream(stream));
 }
