@@ -19,17 +19,29 @@
 //      id and gain) into shared memory;
 //   2. each warp builds its groups' live masks with two ballots and, for a live group,
 //      starts the TMA bulk copies of the group's scale and bias chunks (C*2 bytes each);
-//   3. every warp scans the live counts and compacts its groups' live rows into an
-//      ascending list (ballot prefix popcounts); each lane holding a live row starts the
-//      TMA bulk copy of that row's C/2-byte chunk. All copies of the batch complete on one
-//      mbarrier whose single arrival carries the batch's byte count, so the whole batch is
-//      in flight at once and a copy costs one instruction;
-//   4. thread (word wp, group lane gl) walks the live rows of groups gl, gl+NGL, ... in
-//      shared memory, accumulating acc'[n] = sum h * (1 + q_n/16) and hsum = sum h in fp32,
-//      and folds each group in as out[n] += g * (16*s[n]*(acc'[n] - hsum) + b[n]*hsum) --
-//      the reference's affine algebra (s * sum(h q) + b * sum(h)); 1 + q/16 is built exactly
-//      from the nibble with bit operations, sparing an integer-to-float conversion per weight;
-//   5. the NGL group lanes are reduced in shared memory in a fixed order.
+//   3. every warp scans the live counts, cuts the live rows into sub-batches of whole groups
+//      of at most SBR rows, and compacts its groups' live rows into an ascending list
+//      (ballot prefix popcounts); each lane holding a live row of one of the first `slots`
+//      sub-batches starts the TMA bulk copy of that row's C/2-byte chunk into the
+//      sub-batch's slot of the shared-memory ring. A slot's copies complete on the slot's
+//      mbarrier, whose single arrival carries the sub-batch's byte count, so up to `slots`
+//      sub-batches are in flight at once and a copy costs one instruction;
+//   4. per sub-batch, as its slot's mbarrier completes: thread (word wp, group lane gl)
+//      walks the live rows of its groups gl, gl+NGL, ... of the sub-batch in shared memory,
+//      accumulating acc'[n] = sum h * (1 + q_n/16) and hsum = sum h in fp32, and folds each
+//      group in as out[n] += g * (16*s[n]*(acc'[n] - hsum) + b[n]*hsum) -- the reference's
+//      affine algebra (s * sum(h q) + b * sum(h)); 1 + q/16 is built exactly from the
+//      nibble with bit operations, sparing an integer-to-float conversion per weight. The
+//      computation of a sub-batch overlaps the landing of the later ones; a slot freed is
+//      refilled with the sub-batch `slots` places later;
+//   5. the NGL group lanes are reduced in shared memory in a fixed order;
+//   6. each CTA pushes the 8 slices of its partial chunk to their owner CTAs with st.async
+//      (completing on the owner's mbarrier), and each owner sums its slice's 8 partials in
+//      rank order: one cluster handshake (at the start) instead of two cluster barriers.
+// A lane's groups are folded in ascending order whatever the sub-batch cut, and a group's
+// rows always form one sub-batch, so the result depends neither on the ring's size nor on
+// the other groups' live counts: the dense form (every row live) and the sparse form give
+// the same bits, and so do every stage size chosen per batch size below.
 // Weights are streamed with an L2 evict-first policy (they are not reused by the step).
 // The launch uses programmatic dependent launch: the kernel releases its dependents at
 // once and waits (griddepcontrol.wait) for the previous kernel before its first read, so
@@ -50,14 +62,17 @@ namespace {
 constexpr int kCluster = 8;    // CTAs per (token, chunk)
 constexpr int kGB = 32;        // groups per batch
 constexpr int kGS = 64;        // quantisation group size
+constexpr int kMaxSlots = 8;   // sub-batch slots (mbarriers) of the staging ring
 
 template <int C>
 struct DecodeCfg {
   static constexpr int NWC = C / 8;                    // words of one row in a chunk
   static constexpr int THREADS = 512;                  // 16 full warps (ballots use full masks)
   static constexpr int WARPS = THREADS / 32;
-  static constexpr int NGL = THREADS / NWC;            // group lanes: 32 (C = 128), 21 (C = 192)
-  static constexpr int RB = 1024;                      // staged rows per sub-batch
+  static constexpr int NGL = WARPS;                    // group lanes: one warp each, a lane per word
+  static_assert(NWC <= 32, "a chunk row must fit one warp");
+  static constexpr int MAX_RB = 1024;                  // largest staging ring, in rows
+  static constexpr int MIN_RB = NGL * 8;               // the group-lane partials reuse the ring
 };
 
 struct DecodeParams {
@@ -77,25 +92,36 @@ struct DecodeParams {
   int NR;    // columns of h: topk*F + FS
   int GT;    // groups per token
   int NW;    // words per neuron row: D/8
+  int SBR;   // rows per ring slot = the sub-batch limit (>= 64: a group's rows fit one slot)
+  int nring; // slots of the staging ring (ring rows = SBR * nring), 1..kMaxSlots
 };
 
+// The staging ring (SBR*nring rows of NWC words, also the group-lane partials) follows this
+// struct in dynamic shared memory, at a 128-byte boundary.
 template <int C>
 struct DecodeSmem {
   using Cfg = DecodeCfg<C>;
-  uint32_t stage[Cfg::RB * Cfg::NWC];           // staged row chunks (also the group-lane partials)
   uint16_t meta_s[kGB * C];                     // staged scale chunks (16-bit)
   uint16_t meta_b[kGB * C];                     // staged bias chunks
   float hs[kGB * kGS];                          // the batch's h values (fp32)
   float hrow[kGB * kGS];                        // h of each compacted live row
   uint16_t rows[kGB * kGS];                     // compacted live rows: (group in batch) << 6 | neuron
   unsigned long long gmask[kGB];
-  unsigned long long bar;                       // completion of the batch's bulk copies
+  unsigned long long bars[kMaxSlots];           // completion of each slot's bulk copies
+  unsigned long long rbar;                      // arrival of the 8 partial slices (st.async)
   int gcnt[kGB], goff[kGB + 1];
+  int sbeg[kGB + 1];                            // sub-batch starts (rows); sbeg[nsb] = nrows
   int gsrc[kGB];                                // expert id, -1 = shared expert, -2 = invalid
   int gloc[kGB];                                // the group's index inside its expert
   float ggain[kGB];
   float part[C];                                // this CTA's partial output chunk
+  float recv[C];                                // [rank][C/8]: the slices pushed to this CTA
 };
+
+template <int C>
+constexpr size_t ring_offset() {
+  return (sizeof(DecodeSmem<C>) + 127) / 128 * 128;
+}
 
 // Live mask of 64 h values (two per lane) with two ballots.
 __device__ __forceinline__ unsigned long long ballot64(bool nz0, bool nz1) {
@@ -166,6 +192,33 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
 }
 
+// ---- distributed shared memory helpers
+// The address of this CTA's shared-memory location `a` in cluster CTA `r`.
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t a, uint32_t r) {
+  uint32_t o;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(o) : "r"(a), "r"(r));
+  return o;
+}
+// A 4-byte store into another cluster CTA's shared memory, counted on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_f32(uint32_t addr, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];"
+               ::"r"(addr), "f"(v), "r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait (cluster-scope acquire) for the phase with `parity`: false after ~2 s.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait_cluster(bar, parity))
+    if (global_ns() - t0 > 2000000000ull) return false;
+  return true;
+}
+
 template <typename HT, typename ST, typename YT, int C>
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>::THREADS)
     sparse_down_decode_kernel(const DecodeParams p) {
@@ -185,25 +238,36 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
   const int GF = p.F / kGS;
   const int g_lo = static_cast<int>((static_cast<long long>(rank) * p.GT) / kCluster);
   const int g_hi = static_cast<int>((static_cast<long long>(rank + 1) * p.GT) / kCluster);
-  const int wp = tid % NWC;                       // word of the chunk this thread owns
-  const int gl = tid / NWC;                       // group lane
-  const bool lane_used = gl < NGL;                // (C = 192: threads 504..511 idle)
-  const bool active = lane_used && wp < nwc;
-  constexpr int RB = Cfg::RB;
-  const uint32_t bar = smem_u32(&S.bar);
+  // A group lane is a warp and its lane wp owns word wp of the chunk: the lanes of a warp
+  // walk the same rows, so the row loop never diverges (C = 192: lanes 24..31 idle).
+  const int wp = lane;                            // word of the chunk this thread owns
+  const int gl = warp;                            // group lane
+  const bool lane_used = wp < NWC;
+  const bool active = wp < nwc;
+  uint32_t* ring = reinterpret_cast<uint32_t*>(smem_raw + ring_offset<C>());
+  const int SBR = p.SBR, nring = p.nring;
+  const uint32_t bar0 = smem_u32(&S.bars[0]);     // slot k's mbarrier: bar0 + 8*k
+  const uint32_t rbar = smem_u32(&S.rbar);
   const uint32_t meta_bytes = static_cast<uint32_t>(nwc) * 16;   // 8 outputs x 2 bytes per word
   const uint32_t row_bytes = static_cast<uint32_t>(nwc) * 4;
-  uint32_t phase = 0;
+  constexpr int per = C / kCluster;               // outputs of the chunk each CTA finishes
+  uint32_t phases = 0;                            // bit k: the parity slot k waits for next
+  const uint64_t pol = evict_first_policy();
 
   if (tid == 0) {
-    mbar_init(bar, 1);
+    for (int k = 0; k < kMaxSlots; ++k) mbar_init(bar0 + 8u * k, 1);
+    mbar_init(rbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // the 8 slices of C/8 partials that the cluster's CTAs push here complete this phase
+    mbar_arrive_expect_tx(rbar, static_cast<uint32_t>(sizeof(float) * C));
   }
+  __syncthreads();
+  // the handshake that makes every CTA's mbarriers visible before any push (waited in 6.)
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   // Programmatic dependent launch: let the next kernel in the stream start its launch
   // now, and wait for the previous one (which produces h / sel / gains) before reading.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const uint64_t pol = evict_first_policy();
 
   float out[8];
 #pragma unroll
@@ -220,8 +284,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
       for (int v = tid; v < ng * kGS / HPV; v += THREADS) {
         const uint4 raw = __ldg(reinterpret_cast<const uint4*>(hrow) + v);
         const HT* e = reinterpret_cast<const HT*>(&raw);
+        float f[HPV];
 #pragma unroll
-        for (int i = 0; i < HPV; ++i) S.hs[v * HPV + i] = hsd::to_f32<HT>(e[i]);
+        for (int i = 0; i < HPV; ++i) f[i] = hsd::to_f32<HT>(e[i]);
+#pragma unroll
+        for (int i = 0; i < HPV; i += 4)
+          *reinterpret_cast<float4*>(&S.hs[v * HPV + i]) = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
       }
       if (tid < ng) {
         const int G = gb0 + tid;
@@ -260,13 +328,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
         const int64_t grow = (src >= 0) ? static_cast<int64_t>(src) * GF + S.gloc[gi] : S.gloc[gi];
         const uint16_t* base = (src >= 0) ? (lane ? p.pb : p.ps) : (lane ? p.spb : p.sps);
         bulk_g2s((lane ? S.meta_b : S.meta_s) + gi * C, base + grow * p.D + static_cast<int64_t>(w0) * 8,
-                 meta_bytes, bar, pol);
+                 meta_bytes, bar0, pol);                 // with sub-batch 0, on slot 0
       }
     }
     __syncthreads();
-    // ---- 3. the counts' exclusive scan (every warp, redundantly), the compaction and the
-    //         row copies of the first sub-batch
-    int nrows, first_rows;
+    // ---- 3. the counts' exclusive scan and the sub-batch cut (every warp, redundantly),
+    //         the compaction and the row copies of the first nring sub-batches
+    int nsb = 0;
     {
       const int c = (lane < ng) ? S.gcnt[lane] : 0;
       int x = c;
@@ -275,29 +343,43 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
         const int y = __shfl_up_sync(0xffffffffu, x, d);
         if (lane >= d) x += y;
       }
-      const int goff_lane = x - c;
-      nrows = __shfl_sync(0xffffffffu, x, 31);
-      // sub-batches end on group boundaries (the last group start or end <= RB), so no
-      // group is ever folded in two pieces: a group's sum is the same sequence of fp32
-      // operations whatever the other groups' live counts, and the dense form (all rows
-      // live, zeros included) reproduces the sparse form bit for bit
-      const unsigned cand = (lane < ng && goff_lane <= RB) ? static_cast<unsigned>(goff_lane) : 0u;
-      const unsigned first_end = max(__reduce_max_sync(0xffffffffu, cand),
-                                     nrows <= RB ? static_cast<unsigned>(nrows) : 0u);
-      first_rows = static_cast<int>(first_end);
+      const int goff_lane = x - c;                 // group `lane`'s rows: [goff_lane, x)
+      const int nrows = __shfl_sync(0xffffffffu, x, 31);
+      // greedy cut into sub-batches of whole groups of at most SBR rows (a group never
+      // straddles two, so it is always folded in one piece: a group's sum is the same
+      // sequence of fp32 operations whatever the other groups' live counts). Lane k ends
+      // holding sub-batch k's first row (my_sbeg) and last row + 1 (my_send); my_sb is the
+      // sub-batch of group `lane`.
+      int my_sbeg = 0, my_sb = 0;
+      for (int start = 0; start < nrows; ++nsb) {
+        const unsigned cand = (lane < ng && x > start && x - start <= SBR) ? static_cast<unsigned>(x) : 0u;
+        const int nxt = static_cast<int>(__reduce_max_sync(0xffffffffu, cand));
+        if (lane == nsb) my_sbeg = start;
+        if (lane < ng && goff_lane >= start && goff_lane < nxt) my_sb = nsb;
+        start = nxt;
+      }
+      if (lane == nsb) my_sbeg = nrows;
+      const int next_beg = __shfl_down_sync(0xffffffffu, my_sbeg, 1);
+      const int my_send = (lane + 1 >= nsb) ? nrows : next_beg;
       if (warp == 0) {
         if (lane < ng) S.goff[lane] = goff_lane;
         if (lane == 0) S.goff[ng] = nrows;
-        // the batch's whole byte count, registered once with the single arrival (copies
-        // already issued may complete first: the phase cannot end before the arrival)
+        if (lane < nsb) S.sbeg[lane] = my_sbeg;
+        if (lane == 0) S.sbeg[nsb] = nrows;
+        // each in-flight sub-batch's byte count, registered once with its slot's single
+        // arrival (copies already issued may complete first: the phase cannot end before
+        // the arrival); slot 0 also carries the batch's scale/bias chunks
         const unsigned live_groups = __popc(__ballot_sync(0xffffffffu, c > 0));
-        if (lane == 0 && nrows > 0)
-          mbar_arrive_expect_tx(bar, (p.loadsc ? live_groups * 2u * meta_bytes : 0u) +
-                                         first_end * row_bytes);
+        if (lane < min(nsb, nring))
+          mbar_arrive_expect_tx(bar0 + 8u * lane,
+                                static_cast<uint32_t>(my_send - my_sbeg) * row_bytes +
+                                    ((lane == 0 && p.loadsc) ? live_groups * 2u * meta_bytes : 0u));
       }
       for (int gi = warp; gi < ng; gi += WARPS) {
         const unsigned long long m = S.gmask[gi];
         const int base = __shfl_sync(0xffffffffu, goff_lane, gi);
+        const int sb = __shfl_sync(0xffffffffu, my_sb, gi);
+        const int sb_first = __shfl_sync(0xffffffffu, my_sbeg, sb & 31);
         const int src = S.gsrc[gi];
         const int64_t rowbase = (src >= 0) ? (static_cast<int64_t>(src) * p.F + static_cast<int64_t>(S.gloc[gi]) * kGS)
                                            : static_cast<int64_t>(S.gloc[gi]) * kGS;
@@ -309,52 +391,37 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
             const int idx = base + live_prefix(m, j);
             S.rows[idx] = static_cast<uint16_t>((gi << 6) | j);
             S.hrow[idx] = S.hs[gi * kGS + j];
-            if (idx < first_rows) bulk_g2s(&S.stage[idx * NWC], wbase + (rowbase + j) * p.NW + w0, row_bytes, bar, pol);
+            if (sb < nring)
+              bulk_g2s(ring + static_cast<size_t>(sb * SBR + idx - sb_first) * NWC, wbase + (rowbase + j) * p.NW + w0,
+                       row_bytes, bar0 + 8u * sb, pol);
           }
         }
       }
     }
     __syncthreads();
 
-    // ---- 4. per sub-batch of at most RB rows and whole groups: wait for the copies,
-    //         accumulate from shared memory
-    for (int r0 = 0, r1 = first_rows; r0 < nrows; r0 = r1) {
-      if (r0 > 0) {                              // the next group boundary within RB rows
-        r1 = r0;
-        for (int g = 0; g <= ng; ++g) {
-          const int o = S.goff[g];
-          if (o > r1 && o - r0 <= RB) r1 = o;
-        }
-      }
-      const int rn = r1 - r0;
-      if (r0 > 0) {                              // later sub-batches (dense h only)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        if (tid == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(rn) * row_bytes);
-        for (int r = tid; r < rn; r += THREADS) {
-          const int code = S.rows[r0 + r];
-          const int gi = code >> 6, j = code & 63;
-          const int src = S.gsrc[gi];
-          const int64_t neuron = static_cast<int64_t>(S.gloc[gi]) * kGS + j;
-          const uint32_t* g = (src >= 0) ? p.pw + (static_cast<int64_t>(src) * p.F + neuron) * p.NW
-                                         : p.spw + neuron * p.NW;
-          bulk_g2s(&S.stage[r * NWC], g + w0, row_bytes, bar, pol);
-        }
-      }
-      if (!mbar_wait_bounded(bar, phase)) {
+    // ---- 4. per sub-batch, as its slot's copies land: accumulate from shared memory, then
+    //         refill the slot with the sub-batch nring places later
+    for (int k = 0; k < nsb; ++k) {
+      const int r0 = S.sbeg[k], r1 = S.sbeg[k + 1];
+      const int sk = k % nring;
+      const uint32_t bk = bar0 + 8u * sk;
+      const uint32_t* stage = ring + static_cast<size_t>(sk) * SBR * NWC;
+      if (!mbar_wait_bounded(bk, (phases >> sk) & 1u)) {
         if (tid == 0) hsd_flag_decode(HSD_ERR_TIMEOUT);
-        mbar_wait_bounded(bar, phase);           // once more for the copies still in flight
+        mbar_wait_bounded(bk, (phases >> sk) & 1u);   // once more for the copies still in flight
       }
-      phase ^= 1u;
+      phases ^= 1u << sk;
       if (active) {
         for (int gi = gl; gi < ng; gi += NGL) {
-          const int j0 = max(S.goff[gi], r0), j1 = min(S.goff[gi + 1], r0 + rn);
+          const int j0 = max(S.goff[gi], r0), j1 = min(S.goff[gi + 1], r1);
           if (j0 >= j1) continue;
           float acc[8], hsum = 0.f;
 #pragma unroll
           for (int n = 0; n < 8; ++n) acc[n] = 0.f;
           for (int r = j0; r < j1; ++r) {
             const float hv = S.hrow[r];
-            const uint32_t q = S.stage[(r - r0) * NWC + wp];
+            const uint32_t q = stage[(r - r0) * NWC + wp];
             hsum += hv;
             acc[0] = fmaf(hv, nib_unit<0>(q), acc[0]);
             acc[1] = fmaf(hv, nib_unit<1>(q), acc[1]);
@@ -383,14 +450,27 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
           }
         }
       }
-      __syncthreads();                           // stage / meta / hs are rewritten next
+      if (k + nring < nsb) {                     // refill slot sk (every thread is done with it)
+        __syncthreads();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const int q0 = S.sbeg[k + nring], qn = S.sbeg[k + nring + 1] - q0;
+        if (tid == 0) mbar_arrive_expect_tx(bk, static_cast<uint32_t>(qn) * row_bytes);
+        for (int r = tid; r < qn; r += THREADS) {
+          const int code = S.rows[q0 + r];
+          const int gi = code >> 6, j = code & 63;
+          const int src = S.gsrc[gi];
+          const int64_t neuron = static_cast<int64_t>(S.gloc[gi]) * kGS + j;
+          const uint32_t* g = (src >= 0) ? p.pw + (static_cast<int64_t>(src) * p.F + neuron) * p.NW
+                                         : p.spw + neuron * p.NW;
+          bulk_g2s(ring + (static_cast<size_t>(sk) * SBR + r) * NWC, g + w0, row_bytes, bk, pol);
+        }
+      }
     }
+    __syncthreads();                             // the ring, meta and hs are rewritten next
   }
 
-  // ---- 5. reduce the group lanes (fixed order) into S.part, reusing the stage buffer
-  float* red = reinterpret_cast<float*>(S.stage);   // [NGL][C] fp32
-  static_assert(sizeof(float) * Cfg::NGL * C <= sizeof(uint32_t) * Cfg::RB * Cfg::NWC,
-                "group-lane reduction must fit in the stage buffer");
+  // ---- 5. reduce the group lanes (fixed order) into S.part, reusing the ring
+  float* red = reinterpret_cast<float*>(ring);   // [NGL][C] fp32 (the host keeps ring >= MIN_RB rows)
   if (lane_used) {
     *reinterpret_cast<float4*>(&red[gl * C + wp * 8]) = make_float4(out[0], out[1], out[2], out[3]);
     *reinterpret_cast<float4*>(&red[gl * C + wp * 8 + 4]) = make_float4(out[4], out[5], out[6], out[7]);
@@ -410,21 +490,32 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
     for (int o = tid; o < C; o += THREADS)
       S.part[o] = (red2[o] + red2[C + o]) + (red2[2 * C + o] + red2[3 * C + o]);
   }
-  // ---- 6. the cluster's 8 partials, summed in rank order through DSMEM
-  cluster.sync();
-  constexpr int per = C / kCluster;
+  // ---- 6. the cluster's 8 partials: slice r of every CTA's chunk goes to CTA r (st.async,
+  //         completing on CTA r's rbar), which sums the 8 slices in rank order
+  __syncthreads();
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // every rbar is initialised
+  for (int o = tid; o < C; o += THREADS) {
+    const int dst = o / per;
+    st_async_f32(mapa_u32(smem_u32(&S.recv[rank * per + (o - dst * per)]), dst), S.part[o],
+                 mapa_u32(rbar, dst));
+  }
+  if (!mbar_wait_cluster_bounded(rbar, 0)) {
+    if (tid == 0) hsd_flag_decode(HSD_ERR_TIMEOUT);
+    mbar_wait_cluster_bounded(rbar, 0);          // once more for the stores still in flight
+  }
   for (int i = tid; i < per; i += THREADS) {
     const int o = rank * per + i;
     if (o < nwc * 8) {
       float t = 0.f;
 #pragma unroll
-      for (int q = 0; q < kCluster; ++q) t += cluster.map_shared_rank(S.part, q)[o];
+      for (int q = 0; q < kCluster; ++q) t += S.recv[q * per + i];
       const int64_t yi = static_cast<int64_t>(b) * p.D + static_cast<int64_t>(w0) * 8 + o;
       if (p.resid) t += hsd::to_f32<YT>(reinterpret_cast<const YT*>(p.resid)[yi]);
       reinterpret_cast<YT*>(p.y)[yi] = hsd::from_f32<YT>(t);
     }
   }
-  cluster.sync();                                // keep this CTA's smem alive for the readers
+  // No CTA reads another's shared memory, and every CTA leaves only after the 8 slices
+  // pushed to it have landed, so no closing cluster barrier is needed.
 }
 
 // ---- active-index sets, the same ballot compaction per (token, slot)
@@ -470,17 +561,41 @@ __global__ void __launch_bounds__(kLiveThreads) live_rows_kernel(const void* h, 
   if (threadIdx.x == 0) count[static_cast<int64_t>(b) * (topk + 1) + slot] = base_s;
 }
 
+// The staging ring per launch (measured on B200, 23 layers, z = 0.90): one token stages up to
+// 1024 rows in one slot (145 KB of shared memory: one CTA per SM, the 112 CTAs of a token
+// never share an SM); larger batches stage 256 rows in one slot (72 KB: three CTAs share an
+// SM, so a verify step of 3 rows runs in one wave: 24 -> 14 us a layer at B = 3, 48 -> 33 us
+// at B = 8). Splitting the same rows into 2-8 pipelined slots measured slower at every batch
+// size: the copies of a sub-batch land together, and each extra wait costs more than the
+// overlap gains. HSD_DECODE_SBR / HSD_DECODE_RING force the slot rows / slot count.
+inline void ring_choice(int B, int min_rb, int* sbr, int* nring) {
+  static const int forced_sbr = [] { const char* e = getenv("HSD_DECODE_SBR"); return e ? atoi(e) : 0; }();
+  static const int forced_ring = [] { const char* e = getenv("HSD_DECODE_RING"); return e ? atoi(e) : 0; }();
+  *sbr = B == 1 ? 1024 : 256;
+  *nring = 1;
+  if (forced_sbr >= 64 && forced_sbr <= 1024) *sbr = forced_sbr;
+  if (forced_ring >= 1 && forced_ring <= kMaxSlots) *nring = forced_ring;
+  while (*sbr * *nring < min_rb || *sbr * *nring > 1024) {
+    if (*sbr * *nring < min_rb) ++*nring; else --*nring;
+    if (*nring > kMaxSlots) { *nring = kMaxSlots; *sbr *= 2; }
+    if (*nring < 1) { *nring = 1; *sbr /= 2; }
+  }
+}
+
 template <typename HT, typename ST, typename YT, int C>
-int launch_decode(const DecodeParams& p, cudaStream_t st) {
+int launch_decode(DecodeParams p, cudaStream_t st) {
   using Cfg = DecodeCfg<C>;
   auto kern = sparse_down_decode_kernel<HT, ST, YT, C>;
-  const size_t smem = sizeof(DecodeSmem<C>);
+  static_assert(Cfg::MIN_RB <= Cfg::MAX_RB, "ring bounds");
+  ring_choice(p.B, Cfg::MIN_RB, &p.SBR, &p.nring);
+  const size_t smem = ring_offset<C>() + sizeof(uint32_t) * Cfg::NWC * p.SBR * p.nring;
+  const size_t smem_max = ring_offset<C>() + sizeof(uint32_t) * Cfg::NWC * Cfg::MAX_RB;
   static int configured_device = -1;           // the attribute is set once per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+                                         static_cast<int>(smem_max));
     if (e != cudaSuccess) return hsd::check_cuda(e, "hsd_sparse_down_decode: smem attribute");
     configured_device = dev;
   }
@@ -498,24 +613,28 @@ int launch_decode(const DecodeParams& p, cudaStream_t st) {
   return hsd::check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "hsd_sparse_down_decode launch");
 }
 
-// Output chunk width (outputs per cluster): 192 (112 CTAs per token, one per SM) for
-// B <= 4, where a token's CTAs should not share SMs; 128 (168 CTAs per token) above.
-// HSD_DECODE_CHUNK=128 or 192 forces one for tuning.
+// Output chunk width (outputs per cluster): 192 (112 CTAs per token; one per SM at B = 1) at
+// every batch size -- with three CTAs per SM above B = 1, 192 also beats 128 (168 CTAs per
+// token) at B = 8 (38 vs 46 us a layer). HSD_DECODE_CHUNK=128 forces the narrow form.
 // A token's arithmetic depends on the chunk width only (its groups' lane assignment), so
-// the widths of B = 1 and of verify steps up to 4 rows are the same: a verify row equals the
-// same token decoded alone, bit for bit.
-inline int chunk_choice(int B) {
+// with one width for all batch sizes a row of any batch (a verify row in particular) equals
+// the same token decoded alone, bit for bit.
+inline int chunk_choice(int) {
   static int forced = [] {
     const char* e = getenv("HSD_DECODE_CHUNK");
     return e ? atoi(e) : 0;
   }();
-  if (forced == 128 || forced == 192) return forced;
-  return B <= 4 ? 192 : 128;
+  if (forced == 128 || forced == 192 || forced == 256) return forced;
+  return 192;
 }
 
 template <typename HT, typename ST, typename YT>
 int dispatch_c(const DecodeParams& p, cudaStream_t st) {
-  return chunk_choice(p.B) == 192 ? launch_decode<HT, ST, YT, 192>(p, st) : launch_decode<HT, ST, YT, 128>(p, st);
+  switch (chunk_choice(p.B)) {
+    case 128: return launch_decode<HT, ST, YT, 128>(p, st);
+    case 256: return launch_decode<HT, ST, YT, 256>(p, st);
+  }
+  return launch_decode<HT, ST, YT, 192>(p, st);
 }
 
 template <typename HT, typename ST>

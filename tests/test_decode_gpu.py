@@ -82,7 +82,8 @@ def test_odd_shapes(cuda, dims):
 
 @pytest.mark.gpu
 def test_dense_rows_more_than_one_stage(cuda):
-    """No zeros at all: every row live, so a CTA stages several 512-row sub-batches."""
+    """No zeros at all: every row live (1856 rows a CTA), so a CTA stages its rows in more
+    than one sub-batch of its 1024-row ring."""
     c = synth.decode_case(seed=4, B=1, zero_frac=0.001, device=cuda)
     y = run(c, layouts(c), out_dtype=torch.float32)
     assert rel_err(f32_np(y), oracle_y(c)) < TOL
@@ -186,13 +187,49 @@ def test_dense_form_is_bit_identical(cuda, B, z):
 
 
 @pytest.mark.gpu
-def test_verify_rows_equal_single_tokens(cuda):
-    """A token's output does not depend on the other rows of its launch up to 4 rows (the
-    verify steps of MTP-1..3): rows of a B = 3 launch equal B = 1 launches bit for bit."""
-    c = synth.decode_case(seed=77, B=3, zero_frac=0.9, device=cuda)
+@pytest.mark.parametrize("B", [3, 8])
+def test_verify_rows_equal_single_tokens(cuda, B):
+    """A token's output does not depend on the other rows of its launch (the verify steps
+    of MTP-1..3 in particular), although batches stage their rows in a smaller ring than a
+    single token: rows of a B-row launch equal B = 1 launches bit for bit."""
+    c = synth.decode_case(seed=77, B=B, zero_frac=0.9, device=cuda)
     lay = layouts(c)
-    y3 = run(c, lay, out_dtype=torch.float32)
-    for b in range(3):
+    yb = run(c, lay, out_dtype=torch.float32)
+    for b in range(B):
         y1 = hsd_b200.sparse_down(c["h"][b:b + 1], c["sel"][b:b + 1], c["gains"][b:b + 1], *lay, F=c["F"],
                                   FS=c["FS"], D=c["D"], topk=c["topk"], out_dtype=torch.float32)
-        assert torch.equal(y1[0], y3[b])
+        assert torch.equal(y1[0], yb[b])
+
+
+_RING_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+import hsd_b200
+from hsd_b200 import synth
+dev = torch.device("cuda", 0)
+c = synth.decode_case(seed=91, B=3, zero_frac=0.5, device=dev)
+lay = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"]) + hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
+y = hsd_b200.sparse_down(c["h"], c["sel"], c["gains"], *lay, F=c["F"], FS=c["FS"], D=c["D"], topk=c["topk"],
+                         out_dtype=torch.float32)
+torch.save(y.cpu(), sys.argv[2])
+"""
+
+
+@pytest.mark.gpu
+def test_ring_shape_does_not_change_bits(cuda, tmp_path):
+    """The staging ring's shape (rows per slot, slots in flight; forced through the
+    HSD_DECODE_SBR / HSD_DECODE_RING variables, read once per process) changes how the
+    copies are scheduled, never the arithmetic: 1x256, 4x64 and 2x512 rows give the same bits
+    on a case with ~900 live rows per CTA (several sub-batches, refilled slots)."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    pkg = os.path.join(os.path.dirname(here), "mlx-heimr-sparse-down_b200")
+    outs = []
+    for sbr, ring in ((256, 1), (64, 4), (512, 2)):
+        f = tmp_path / f"y_{sbr}_{ring}.pt"
+        env = dict(os.environ, HSD_DECODE_SBR=str(sbr), HSD_DECODE_RING=str(ring))
+        subprocess.run([sys.executable, "-c", _RING_SCRIPT, pkg, str(f)], env=env, check=True, timeout=300)
+        outs.append(torch.load(f))
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
