@@ -239,7 +239,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
   const int g_lo = static_cast<int>((static_cast<long long>(rank) * p.GT) / kCluster);
   const int g_hi = static_cast<int>((static_cast<long long>(rank + 1) * p.GT) / kCluster);
   // A group lane is a warp and its lane wp owns word wp of the chunk: the lanes of a warp
-  // walk the same rows, so the row loop never diverges (C = 192: lanes 24..31 idle).
+  // walk the same rows, so the row loop never diverges (C < 256 leaves lanes idle).
   const int wp = lane;                            // word of the chunk this thread owns
   const int gl = warp;                            // group lane
   const bool lane_used = wp < NWC;
@@ -561,11 +561,10 @@ __global__ void __launch_bounds__(kLiveThreads) live_rows_kernel(const void* h, 
   if (threadIdx.x == 0) count[static_cast<int64_t>(b) * (topk + 1) + slot] = base_s;
 }
 
-// The staging ring per launch (measured on B200, 23 layers, z = 0.90): one token stages up to
-// 1024 rows in one slot (145 KB of shared memory: one CTA per SM, the 112 CTAs of a token
-// never share an SM); larger batches stage 256 rows in one slot (72 KB: three CTAs share an
-// SM, so a verify step of 3 rows runs in one wave: 24 -> 14 us a layer at B = 3, 48 -> 33 us
-// at B = 8). Splitting the same rows into 2-8 pipelined slots measured slower at every batch
+// The staging ring per launch (measured on B200, 23 layers, z = 0.90, 192-output chunks): one
+// token stages up to 1024 rows in one slot (one CTA per SM: a token's CTAs never share an
+// SM); larger batches stage 256 rows in one slot (several CTAs share an SM, so a verify step
+// of 3 rows runs in one wave: 24 -> 14 us a layer at B = 3, 48 -> 33 us at B = 8). Splitting the same rows into 2-8 pipelined slots measured slower at every batch
 // size: the copies of a sub-batch land together, and each extra wait costs more than the
 // overlap gains. HSD_DECODE_SBR / HSD_DECODE_RING force the slot rows / slot count.
 inline void ring_choice(int B, int min_rb, int* sbr, int* nring) {
@@ -613,19 +612,20 @@ int launch_decode(DecodeParams p, cudaStream_t st) {
   return hsd::check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "hsd_sparse_down_decode launch");
 }
 
-// Output chunk width (outputs per cluster): 192 (112 CTAs per token; one per SM at B = 1) at
-// every batch size -- with three CTAs per SM above B = 1, 192 also beats 128 (168 CTAs per
-// token) at B = 8 (38 vs 46 us a layer). HSD_DECODE_CHUNK=128 forces the narrow form.
-// A token's arithmetic depends on the chunk width only (its groups' lane assignment), so
-// with one width for all batch sizes a row of any batch (a verify row in particular) equals
-// the same token decoded alone, bit for bit.
+// Output chunk width (outputs per cluster): 256 at every batch size -- a chunk row is one
+// warp's 32 words, and at D = 2688 a token is 10 full chunks and a half-width tail (88 CTAs).
+// Measured per layer (B200, 23 layers, z = 0.90) against 192 (14 chunks, 24 of 32 lanes busy):
+// B = 1 7.6 vs 7.7 us, B = 3 10.9 vs 14.1 us, B = 8 30.0 vs 33.0 us. HSD_DECODE_CHUNK=128 or
+// 192 forces a narrower form. A token's arithmetic depends on the chunk width only (which
+// words share a CTA), so with one width for all batch sizes a row of any batch (a verify row
+// in particular) equals the same token decoded alone, bit for bit.
 inline int chunk_choice(int) {
   static int forced = [] {
     const char* e = getenv("HSD_DECODE_CHUNK");
     return e ? atoi(e) : 0;
   }();
   if (forced == 128 || forced == 192 || forced == 256) return forced;
-  return 192;
+  return 256;
 }
 
 template <typename HT, typename ST, typename YT>
