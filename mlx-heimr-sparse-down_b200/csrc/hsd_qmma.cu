@@ -18,6 +18,9 @@
 // The token values are rounded to fp16 (bf16 inputs are exact in fp16 inside its range).
 // An output element depends only on its weight row and its token row, so a token's result
 // does not depend on the other tokens of the launch.
+#include <algorithm>
+#include <cstdlib>
+
 #include "hsd_common.cuh"
 
 HSD_DEFINE_STATUS(qmma)
@@ -277,6 +280,302 @@ __global__ void __launch_bounds__(kThreads) qmma_kernel(const QParams p) {
   }
 }
 
+// ---- the streaming form (B <= 8, every row count a multiple of 16): one persistent block
+// per SM walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...; a tile's 16 weight rows and
+// their scales / biases arrive by TMA bulk copies into a ring of `nst` shared-memory stages
+// (one mbarrier each), so the weights stream while earlier tiles compute, and the token rows
+// are staged once per block. 16 warps split a tile's 64-groups (g = warp, warp+16, ..., two
+// at a time for independent MMA chains) and their partials are summed in warp order.
+// Measured on B200 (CUDA-graph replay, weights rotated through HBM): the 131072 x 2688 lm_head
+// at one row 79 us (2.5 TB/s) against 128 us for the one-tile-per-block form; per tile, one
+// bulk copy of the 16 contiguous rows beat 16 copies of padded rows (TMA time per copy), and
+// 16 warps with two groups in flight beat 8 warps with one.
+constexpr int kStMax = 8;
+constexpr int kSWarps = 16;
+constexpr int kSThreads = kSWarps * 32;
+
+__device__ __forceinline__ uint32_t q_smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ bool q_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait (~2 s of %globaltimer); false when it ran out.
+__device__ __forceinline__ bool q_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (q_try_wait(bar, parity)) return true;
+  uint64_t t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (!q_try_wait(bar, parity)) {
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > 2000000000ull) return false;
+  }
+  return true;
+}
+__device__ __forceinline__ void q_bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                           uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
+}
+
+struct QTile {
+  const uint32_t* W;   // the tile's first weight row
+  const uint16_t* S;   // its scale rows ([16][red/64])
+  const uint16_t* Bz;  // its bias rows
+  int col0, ncols;
+  int64_t y_base, y_col_stride;
+  bool bad;
+};
+
+// Tile t of the launch (the same tiles as qmma_kernel with one column group, B <= 8).
+template <int MODE>
+__device__ __forceinline__ QTile q_tile(const QParams& p, int t, const int* sel_s) {
+  QTile q;
+  const int WR = p.red / 8, GR = p.red / 64;
+  if (MODE == kQUp && t < p.routed_tiles) {
+    const int tiles_f = p.F / kTile;
+    const int bk = t / tiles_f;
+    const int bi = bk / p.topk, k = bk % p.topk;
+    const int r0 = (t % tiles_f) * kTile;
+    const int e = sel_s[bi * p.topk + k];
+    q.bad = e < 0 || e >= p.E;
+    const int64_t row = static_cast<int64_t>(q.bad ? 0 : e) * p.F + r0;
+    q.W = p.uw + row * WR;
+    q.S = p.us + row * GR;
+    q.Bz = p.ub + row * GR;
+    q.col0 = bi;
+    q.ncols = 1;
+    q.y_base = static_cast<int64_t>(bi) * (p.topk * p.F + p.FS) + static_cast<int64_t>(k) * p.F + r0;
+    q.y_col_stride = 0;
+  } else {
+    if (MODE == kQUp) t -= p.routed_tiles;
+    const int r0 = t * kTile;
+    q.bad = false;
+    q.W = p.w + static_cast<int64_t>(r0) * WR;
+    q.S = p.s + static_cast<int64_t>(r0) * GR;
+    q.Bz = p.b + static_cast<int64_t>(r0) * GR;
+    q.col0 = 0;
+    q.ncols = p.B;
+    if (MODE == kQUp) {
+      q.y_base = static_cast<int64_t>(p.topk) * p.F + r0;
+      q.y_col_stride = static_cast<int64_t>(p.topk) * p.F + p.FS;
+    } else {
+      q.y_base = r0;
+      q.y_col_stride = p.FS;
+    }
+  }
+  return q;
+}
+
+struct QStreamCfg {
+  int ntiles, nst;
+  uint32_t stage_bytes;  // one stage: 16 weight rows of red/8 words, then scales, biases
+  uint32_t off_stages;   // byte offsets in dynamic shared memory
+  uint32_t off_bars, off_sel, off_part;
+};
+
+template <int MODE, typename ST>
+__global__ void __launch_bounds__(kSThreads, 1) qstream_kernel(const QParams p, const QStreamCfg sc) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int red = p.red, NG = red / 64, WR = red / 8, GR = red / 64;
+  const int cs = xh_col_stride_u2(red);
+  const int kc = p.B;                                 // every token column is staged (B <= 8)
+  uint2* xh = reinterpret_cast<uint2*>(smem);
+  float* xsum = reinterpret_cast<float*>(smem + static_cast<size_t>(kc) * cs * sizeof(uint2));
+  float* part = reinterpret_cast<float*>(smem + sc.off_part);    // [2][8 warps][16][8]
+  int* sel_s = reinterpret_cast<int*>(smem + sc.off_sel);
+  unsigned char* stages = smem + sc.off_stages;
+  const uint32_t bar0 = q_smem_u32(smem + sc.off_bars);
+  const uint32_t tile_bytes = 16u * static_cast<uint32_t>(WR) * 4u + 2u * 16u * static_cast<uint32_t>(GR) * 2u;
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+
+  if (MODE == kQUp)
+    for (int i = tid; i < p.B * p.topk; i += kSThreads) sel_s[i] = p.sel[i];
+  if (tid == 0)
+    for (int s = 0; s < sc.nst; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8u * s) : "memory");
+  __syncthreads();
+
+  // the producer: tile t into stage s (its 16 weight rows, scale rows and bias rows: 3 copies)
+  auto issue = [&](int t, int s) {
+    const QTile q = q_tile<MODE>(p, t, sel_s);
+    const uint32_t st = q_smem_u32(stages + static_cast<size_t>(s) * sc.stage_bytes);
+    const uint32_t bar = bar0 + 8u * s;
+    asm volatile("{\n .reg .b64 x;\n mbarrier.arrive.expect_tx.shared::cta.b64 x, [%0], %1;\n}"
+                 ::"r"(bar), "r"(tile_bytes) : "memory");
+    q_bulk_g2s(st, q.W, static_cast<uint32_t>(kTile * WR) * 4u, bar, pol);   // 16 contiguous rows
+    const uint32_t sb = st + static_cast<uint32_t>(kTile * WR) * 4u;
+    q_bulk_g2s(sb, q.S, 16u * GR * 2u, bar, pol);
+    q_bulk_g2s(sb + 16u * GR * 2u, q.Bz, 16u * GR * 2u, bar, pol);
+  };
+  if (tid == 0)
+    for (int i = 0; i < sc.nst; ++i) {
+      const int t = blockIdx.x + i * gridDim.x;
+      if (t < sc.ntiles) issue(t, i);
+    }
+
+  // ---- the token rows in fp16, permuted for the B fragment, and their fp32 group sums
+  const int nch = red / 16;
+  for (int t0 = 0; t0 < kc * nch; t0 += kSThreads) {
+    const int t = t0 + tid;
+    float csum = 0.f;
+    if (t < kc * nch) {
+      const int col = t / nch, ch = t % nch;
+      const int64_t xb = static_cast<int64_t>(col) * p.x_stride + ch * 16;
+      __half hv[16];
+      if (p.x_dtype == HSD_BF16 && (reinterpret_cast<uintptr_t>(static_cast<const uint16_t*>(p.x) + xb) & 15) == 0) {
+        const uint4 r0v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xb));
+        const uint4 r1v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + xb) + 1);
+        const uint32_t wd[8] = {r0v.x, r0v.y, r0v.z, r0v.w, r1v.x, r1v.y, r1v.z, r1v.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          hv[2 * i] = __float2half_rn(__uint_as_float(wd[i] << 16));
+          hv[2 * i + 1] = __float2half_rn(__uint_as_float(wd[i] & 0xffff0000u));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) hv[i] = __float2half_rn(load_f(p.x, p.x_dtype, xb + i));
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        uint2 v;
+        v.x = static_cast<uint32_t>(__half_as_ushort(hv[cc])) | (static_cast<uint32_t>(__half_as_ushort(hv[cc + 4])) << 16);
+        v.y = static_cast<uint32_t>(__half_as_ushort(hv[cc + 8])) | (static_cast<uint32_t>(__half_as_ushort(hv[cc + 12])) << 16);
+        xh[col * cs + ch * 4 + cc] = v;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) csum += __half2float(hv[i]);
+    }
+    csum += __shfl_xor_sync(0xffffffffu, csum, 1);
+    csum += __shfl_xor_sync(0xffffffffu, csum, 2);
+    if (t < kc * nch && (t & 3) == 0) xsum[(t / nch) * NG + (t % nch) / 4] = csum;
+  }
+  __syncthreads();
+
+  const int sh = 4 * c;
+  for (int i = 0;; ++i) {
+    const int t = blockIdx.x + i * gridDim.x;
+    if (t >= sc.ntiles) break;
+    const int s = i % sc.nst;
+    const QTile q = q_tile<MODE>(p, t, sel_s);
+    const uint32_t* sw = reinterpret_cast<const uint32_t*>(stages + static_cast<size_t>(s) * sc.stage_bytes);
+    const uint16_t* sS = reinterpret_cast<const uint16_t*>(sw + kTile * WR);
+    const uint16_t* sB = sS + 16 * GR;
+    if (!q_wait_bounded(bar0 + 8u * s, static_cast<uint32_t>(i / sc.nst) & 1u)) {
+      if (tid == 0) hsd_flag_qmma(HSD_ERR_TIMEOUT);
+      q_wait_bounded(bar0 + 8u * s, static_cast<uint32_t>(i / sc.nst) & 1u);   // copies in flight
+    }
+    const int gq = q.col0 + min(g, q.ncols - 1);
+    const int xc0 = q.col0 + min(2 * c, q.ncols - 1), xc1 = q.col0 + min(2 * c + 1, q.ncols - 1);
+    float y0 = 0.f, y1 = 0.f, y2 = 0.f, y3 = 0.f;
+#pragma unroll 2
+    for (int gr = warp; gr < NG; gr += kSWarps) {
+      const uint4 a0 = *reinterpret_cast<const uint4*>(sw + g * WR + gr * 8);
+      const uint4 a1 = *reinterpret_cast<const uint4*>(sw + g * WR + gr * 8 + 4);
+      const uint4 b0 = *reinterpret_cast<const uint4*>(sw + (g + 8) * WR + gr * 8);
+      const uint4 b1 = *reinterpret_cast<const uint4*>(sw + (g + 8) * WR + gr * 8 + 4);
+      const uint32_t wa_[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const uint32_t wb_[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t a[4] = {nib_pair(wa_[2 * j], sh), nib_pair(wb_[2 * j], sh), nib_pair(wa_[2 * j + 1], sh),
+                               nib_pair(wb_[2 * j + 1], sh)};
+        const uint2 bx = xh[gq * cs + (gr * 4 + j) * 4 + c];
+        mma16816(d, a, bx.x, bx.y);
+      }
+      const float sa = hsd::bits16_to_f32<ST>(sS[g * GR + gr]), sb = hsd::bits16_to_f32<ST>(sS[(g + 8) * GR + gr]);
+      const float ba = hsd::bits16_to_f32<ST>(sB[g * GR + gr]), bb = hsd::bits16_to_f32<ST>(sB[(g + 8) * GR + gr]);
+      const float xs0 = xsum[xc0 * NG + gr], xs1 = xsum[xc1 * NG + gr];
+      y0 = fmaf(sa, d[0], fmaf(ba, xs0, y0));
+      y1 = fmaf(sa, d[1], fmaf(ba, xs1, y1));
+      y2 = fmaf(sb, d[2], fmaf(bb, xs0, y2));
+      y3 = fmaf(sb, d[3], fmaf(bb, xs1, y3));
+    }
+    float* pw = part + ((i & 1) * kSWarps + warp) * (kTile * kCols);
+    pw[g * kCols + 2 * c] = y0;
+    pw[g * kCols + 2 * c + 1] = y1;
+    pw[(g + 8) * kCols + 2 * c] = y2;
+    pw[(g + 8) * kCols + 2 * c + 1] = y3;
+    __syncthreads();                                  // stage s read by every warp; partials written
+    if (tid == 0 && t + sc.nst * static_cast<int>(gridDim.x) < sc.ntiles) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(t + sc.nst * gridDim.x, s);
+    }
+    const float* pt = part + (i & 1) * kSWarps * (kTile * kCols);
+    if (q.bad && tid == 0) hsd_flag_qmma(HSD_ERR_INDEX);
+    for (int e = tid; e < kTile * kCols; e += kSThreads) {
+      const int row = e / kCols, col = e % kCols;
+      if (col >= q.ncols) continue;
+      float acc = 0.f;
+#pragma unroll
+      for (int w8 = 0; w8 < kSWarps; ++w8) acc += pt[w8 * (kTile * kCols) + e];
+      const int64_t yi = q.y_base + static_cast<int64_t>(q.col0 + col) * q.y_col_stride + row;
+      if (MODE == kQUp) {
+        const float v = q.bad ? 0.f : fmaxf(acc, 0.f);
+        store_f(p.y, p.y_dtype, yi, v * v);
+      } else {
+        const float rv = p.resid ? load_f(p.resid, p.y_dtype, yi) : 0.f;
+        store_f(p.y, p.y_dtype, yi, rv + acc);
+      }
+    }
+  }
+}
+
+// The streaming form's shared-memory plan: false when it does not apply (B > 8, a row count
+// that is not a multiple of 16, or fewer than two stages fit), or when HSD_QMMA_STREAM=0.
+bool qstream_plan(const QParams& p, int ntiles, QStreamCfg* sc, size_t* smem) {
+  static const bool disabled = [] { const char* e = getenv("HSD_QMMA_STREAM"); return e && atoi(e) == 0; }();
+  if (disabled || p.B < 1 || p.B > kCols || p.red % 64 != 0 || ntiles < 1) return false;
+  if ((p.routed_tiles > 0 && p.F % kTile != 0) || p.FS % kTile != 0) return false;
+  const size_t WR = p.red / 8, GR = p.red / 64;
+  size_t off = static_cast<size_t>(p.B) * xh_col_stride_u2(p.red) * sizeof(uint2) + p.B * GR * sizeof(float);
+  off = (off + 15) / 16 * 16;
+  sc->off_part = static_cast<uint32_t>(off);
+  off += 2 * kSWarps * kTile * kCols * sizeof(float);
+  sc->off_sel = static_cast<uint32_t>(off);
+  off += 64 * sizeof(int);
+  sc->off_bars = static_cast<uint32_t>(off);
+  off += kStMax * 8;
+  off = (off + 127) / 128 * 128;
+  sc->off_stages = static_cast<uint32_t>(off);
+  const size_t stage = ((kTile * WR * 4 + 2 * kTile * GR * 2) + 127) / 128 * 128;
+  constexpr size_t kBudget = 200 * 1024;
+  if (off + 2 * stage > kBudget || p.B * p.topk > 64) return false;
+  const int nst = static_cast<int>(std::min<size_t>(kStMax, (kBudget - off) / stage));
+  sc->ntiles = ntiles;
+  sc->nst = nst;
+  sc->stage_bytes = static_cast<uint32_t>(stage);
+  *smem = off + nst * stage;
+  return true;
+}
+
+template <int MODE, typename ST>
+int launch_qstream(const QParams& p, const QStreamCfg& sc, size_t smem, cudaStream_t st, const char* who) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms < 1) sms = 1;
+  }
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(qstream_kernel<MODE, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024);
+    if (e != cudaSuccess) return hsd::check_cuda(e, who);
+    configured = true;
+  }
+  const int grid = std::min(sc.ntiles, sms);
+  qstream_kernel<MODE, ST><<<grid, kSThreads, smem, st>>>(p, sc);
+  return hsd::check_launch(who);
+}
+
 // shared memory for `cols` token columns (min(B, 8))
 size_t qmma_smem(int red, int cols) {
   return static_cast<size_t>(cols) * xh_col_stride_u2(red) * sizeof(uint2) + cols * (red / 64) * sizeof(float) +
@@ -299,6 +598,8 @@ int launch_qmma(const QParams& p, int grid, cudaStream_t st, const char* who) {
 
 namespace hsd {
 
+inline bool aligned16(const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
+
 // The MoE up projections with relu2 on the tensor cores (hsd_moe_up_decode's arguments).
 int qmma_moe_up(const void* x, int x_dtype, int64_t x_stride, const int32_t* sel, const uint32_t* uw,
                 const void* us, const void* ub, int s_dtype, const uint32_t* suw, const void* sus, const void* sub,
@@ -314,6 +615,13 @@ int qmma_moe_up(const void* x, int x_dtype, int64_t x_stride, const int32_t* sel
   p.shared_tiles = FS > 0 ? ((FS + kTile - 1) / kTile) * p.col_groups : 0;
   const int64_t grid = static_cast<int64_t>(p.routed_tiles) + p.shared_tiles;
   if (grid > 0x7fffffff) return set_error(HSD_ERR_SHAPE, "hsd_moe_up_decode: grid too large");
+  QStreamCfg sc;
+  size_t smem = 0;
+  const bool al = aligned16(uw) && aligned16(us) && aligned16(ub) && aligned16(suw) && aligned16(sus) &&
+                  aligned16(sub);
+  if (al && qstream_plan(p, static_cast<int>(grid), &sc, &smem))
+    return s_dtype == HSD_BF16 ? launch_qstream<kQUp, __nv_bfloat16>(p, sc, smem, st, "hsd_moe_up_decode")
+                               : launch_qstream<kQUp, __half>(p, sc, smem, st, "hsd_moe_up_decode");
   return s_dtype == HSD_BF16 ? launch_qmma<kQUp, __nv_bfloat16>(p, static_cast<int>(grid), st, "hsd_moe_up_decode")
                              : launch_qmma<kQUp, __half>(p, static_cast<int>(grid), st, "hsd_moe_up_decode");
 }
@@ -331,6 +639,11 @@ int qmma_linear(const void* x, int x_dtype, int64_t x_stride, const uint32_t* w,
   p.col_groups = (B + kCols - 1) / kCols;
   p.shared_tiles = ((out_f + kTile - 1) / kTile) * p.col_groups;
   if (static_cast<int64_t>(p.shared_tiles) > 0x7fffffff) return set_error(HSD_ERR_SHAPE, "hsd_qlinear_decode: grid too large");
+  QStreamCfg sc;
+  size_t smem = 0;
+  if (aligned16(w) && aligned16(s) && aligned16(b) && qstream_plan(p, p.shared_tiles, &sc, &smem))
+    return s_dtype == HSD_BF16 ? launch_qstream<kQLinear, __nv_bfloat16>(p, sc, smem, st, "hsd_qlinear_decode")
+                               : launch_qstream<kQLinear, __half>(p, sc, smem, st, "hsd_qlinear_decode");
   return s_dtype == HSD_BF16 ? launch_qmma<kQLinear, __nv_bfloat16>(p, p.shared_tiles, st, "hsd_qlinear_decode")
                              : launch_qmma<kQLinear, __half>(p, p.shared_tiles, st, "hsd_qlinear_decode");
 }

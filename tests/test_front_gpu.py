@@ -233,3 +233,48 @@ def test_qlinear_rows_equal_single_rows(cuda, B):
     for r in range(B):
         y1 = qlinear(x[r:r + 1], w, s, b, resid=resid[r:r + 1])
         assert torch.equal(y1[0], yb[r])
+
+
+_FORMS_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+from hsd_b200 import synth
+from hsd_b200.front import moe_up, qlinear
+dev = torch.device("cuda", 0)
+out = {}
+for B in (1, 3, 8):
+    gen = torch.Generator(device=dev).manual_seed(300 + B)
+    uw, us, ub = synth.quantized_weights((16, 256, 2688), gen, dev)
+    suw, sus, sub = synth.quantized_weights((512, 2688), gen, dev)
+    x = torch.randn((B, 2688), generator=gen, device=dev).to(torch.bfloat16)
+    sel, _ = synth.route_topk(torch.randn((B, 16), generator=gen, device=dev), 6)
+    out[f"up{B}"] = moe_up(x, sel.to(torch.int32).contiguous(), uw, us, ub, suw, sus, sub, F=256, FS=512, D=2688,
+                           topk=6, out_dtype=torch.float32).cpu()
+    w, s, b = synth.quantized_weights((1040, 2688), gen, dev)
+    resid = torch.randn((B, 1040), generator=gen, device=dev).to(torch.bfloat16)
+    out[f"lin{B}"] = qlinear(x, w, s, b, resid=resid).cpu()
+torch.save(out, sys.argv[2])
+"""
+
+
+@pytest.mark.gpu
+def test_streaming_form_agrees_with_block_form(cuda, tmp_path):
+    """The streaming form of the 4-bit tensor-core products (persistent blocks fed by bulk
+    copies, used for up to 8 rows) and the one-tile-per-block form (HSD_QMMA_STREAM=0, read
+    once per process) compute the same exact per-group MMA sums and differ only in how the
+    fp32 group terms are split over warps: they agree to fp32 rounding, for the MoE up
+    projections and a plain linear, at 1, 3 and 8 rows."""
+    import os
+    import subprocess
+    import sys
+    pkg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "mlx-heimr-sparse-down_b200")
+    outs = []
+    for stream in ("1", "0"):
+        f = tmp_path / f"forms_{stream}.pt"
+        env = dict(os.environ, HSD_QMMA_STREAM=stream)
+        subprocess.run([sys.executable, "-c", _FORMS_SCRIPT, pkg, str(f)], env=env, check=True, timeout=300)
+        outs.append(torch.load(f))
+    for k in outs[0]:
+        a, b = outs[0][k].float(), outs[1][k].float()
+        tol = 1e-5 if k.startswith("up") else 1e-2     # the linear's output is bf16 (one rounding)
+        assert float((a - b).abs().max()) <= tol * float(b.abs().max()), k
