@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(kThreads) attn_chunk_kernel(const __nv_bfloat1
                                                               const __nv_bfloat16* __restrict__ vc,
                                                               const int64_t* pos, int QH, int KVH, int max_len,
                                                               int nsplit, float scale, float* ws) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   constexpr int kRowPad = kHD + 8;  // bf16 per staged K / V row (16-byte skew between rows)
   __shared__ __align__(16) __nv_bfloat16 ks[kChunk * kRowPad];
   __shared__ __align__(16) __nv_bfloat16 vs[kChunk * kRowPad];
@@ -149,6 +151,8 @@ __global__ void __launch_bounds__(kThreads) attn_chunk_kernel(const __nv_bfloat1
 template <int kHD>
 __global__ void __launch_bounds__(kHD) attn_merge_kernel(const float* __restrict__ ws, const int64_t* pos, int QH,
                                                         int max_len, int nsplit, __nv_bfloat16* out) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   const int h = blockIdx.x, l = blockIdx.y, d = threadIdx.x;
   const int n = keys_of_row(pos, l, max_len);
   const int ns = (n + kChunk - 1) / kChunk;
@@ -191,17 +195,17 @@ extern "C" int hsd_attn_decode(const void* q, int64_t q_stride, const void* kc, 
   const auto* vb = static_cast<const __nv_bfloat16*>(vc);
   auto* ob = static_cast<__nv_bfloat16*>(out);
   if (HD == 128) {
-    attn_chunk_kernel<128><<<dim3(nsplit, KVH, L), kThreads, 0, st>>>(qb, q_stride, kb, vb, pos, QH, KVH, max_len,
+    hsd::launch_pdl(attn_chunk_kernel<128>, dim3(nsplit, KVH, L), dim3(kThreads), 0, st, qb, q_stride, kb, vb, pos, QH, KVH, max_len,
                                                                         nsplit, scale, ws);
     int rc = hsd::check_launch(who);
     if (rc != HSD_OK) return rc;
-    attn_merge_kernel<128><<<dim3(QH, L), 128, 0, st>>>(ws, pos, QH, max_len, nsplit, ob);
+    hsd::launch_pdl(attn_merge_kernel<128>, dim3(QH, L), dim3(128), 0, st, ws, pos, QH, max_len, nsplit, ob);
   } else {
-    attn_chunk_kernel<64><<<dim3(nsplit, KVH, L), kThreads, 0, st>>>(qb, q_stride, kb, vb, pos, QH, KVH, max_len,
+    hsd::launch_pdl(attn_chunk_kernel<64>, dim3(nsplit, KVH, L), dim3(kThreads), 0, st, qb, q_stride, kb, vb, pos, QH, KVH, max_len,
                                                                        nsplit, scale, ws);
     int rc = hsd::check_launch(who);
     if (rc != HSD_OK) return rc;
-    attn_merge_kernel<64><<<dim3(QH, L), 64, 0, st>>>(ws, pos, QH, max_len, nsplit, ob);
+    hsd::launch_pdl(attn_merge_kernel<64>, dim3(QH, L), dim3(64), 0, st, ws, pos, QH, max_len, nsplit, ob);
   }
   return hsd::check_launch(who);
 }

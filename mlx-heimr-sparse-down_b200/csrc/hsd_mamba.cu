@@ -54,6 +54,8 @@ __global__ void __launch_bounds__(256) conv_verify_kernel(const void* conv_in, i
                                                           const void* conv_state, const void* w,
                                                           const void* bias, void* out, void* padded, int L,
                                                           int C, const int* n_keep, int rows) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   constexpr int K = 4;                             // the model's conv kernel (checked on the host)
   const int c = blockIdx.x * 256 + threadIdx.x;
   if (c >= C) return;
@@ -89,6 +91,8 @@ __global__ void __launch_bounds__(256) ssm_verify_kernel(const void* xbc, int64_
                                                          float dt_max, const float* state0, float* states,
                                                          void* y, int L, int H, int P, int G, int N, int last_only,
                                                          const int* n_keep, int rows) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   const int warp_g = (blockIdx.x * 256 + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp_g >= H * P) return;
@@ -138,9 +142,9 @@ int conv_dispatch_out(int out_dtype, dim3 grid, cudaStream_t st, const void* con
                       const void* conv_state, const void* w, const void* bias, void* out, void* padded, int L, int C,
                       const int* n_keep, int rows) {
   switch (out_dtype) {
-    case HSD_F32: conv_verify_kernel<TI, TW, float><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows); break;
-    case HSD_F16: conv_verify_kernel<TI, TW, __half><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows); break;
-    case HSD_BF16: conv_verify_kernel<TI, TW, __nv_bfloat16><<<grid, 256, 0, st>>>(conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows); break;
+    case HSD_F32: hsd::launch_pdl(conv_verify_kernel<TI, TW, float>, dim3(grid), dim3(256), 0, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows); break;
+    case HSD_F16: hsd::launch_pdl(conv_verify_kernel<TI, TW, __half>, dim3(grid), dim3(256), 0, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows); break;
+    case HSD_BF16: hsd::launch_pdl(conv_verify_kernel<TI, TW, __nv_bfloat16>, dim3(grid), dim3(256), 0, st, conv_in, in_stride, conv_state, w, bias, out, padded, L, C, n_keep, rows); break;
     default: return hsd::set_error(HSD_ERR_DTYPE, "hsd_mamba_conv_verify: out_dtype %d", out_dtype);
   }
   return hsd::check_launch("hsd_mamba_conv_verify");
@@ -163,10 +167,10 @@ int ssm_dispatch_n(int N, dim3 grid, cudaStream_t st, const void* xbc, int64_t x
                    float dt_max, const float* state0, float* states, void* y, int L, int H, int P, int G,
                    int last_only, const int* n_keep, int rows) {
   switch (N) {
-    case 32: ssm_verify_kernel<TX, TD, TY, 1><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
-    case 64: ssm_verify_kernel<TX, TD, TY, 2><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
-    case 128: ssm_verify_kernel<TX, TD, TY, 4><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
-    case 256: ssm_verify_kernel<TX, TD, TY, 8><<<grid, 256, 0, st>>>(xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
+    case 32: hsd::launch_pdl(ssm_verify_kernel<TX, TD, TY, 1>, dim3(grid), dim3(256), 0, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
+    case 64: hsd::launch_pdl(ssm_verify_kernel<TX, TD, TY, 2>, dim3(grid), dim3(256), 0, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
+    case 128: hsd::launch_pdl(ssm_verify_kernel<TX, TD, TY, 4>, dim3(grid), dim3(256), 0, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
+    case 256: hsd::launch_pdl(ssm_verify_kernel<TX, TD, TY, 8>, dim3(grid), dim3(256), 0, st, xbc, xbc_stride, dt, dt_stride, A_log, Dp, dt_bias, dt_min, dt_max, state0, states, y, L, H, P, G, N, last_only, n_keep, rows); break;
     default: return hsd::set_error(HSD_ERR_SHAPE, "hsd_mamba_ssm_verify: N must be 32, 64, 128 or 256 (got %d)", N);
   }
   return hsd::check_launch("hsd_mamba_ssm_verify");

@@ -62,6 +62,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __global__ void __launch_bounds__(kThreads) rms_norm_kernel(const void* x, int x_dtype, int64_t x_stride,
                                                              const void* w, int w_dtype, void* y, int y_dtype,
                                                              int D, float eps) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   __shared__ float red[kThreads / 32];
   const int64_t r = blockIdx.x;
   const int64_t xo = r * x_stride;
@@ -83,6 +85,8 @@ template <int NV>
 __global__ void __launch_bounds__(kThreads) rms_norm_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t x_stride,
                                                                   const __nv_bfloat16* __restrict__ w,
                                                                   __nv_bfloat16* __restrict__ y, int D, float eps) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   __shared__ float red[kThreads / 32];
   const int64_t r = blockIdx.x;
   const int nq = D / 8;
@@ -125,6 +129,8 @@ __global__ void __launch_bounds__(kThreads) gated_rms_norm_kernel(const void* yv
                                                                    const void* gate, int g_dtype, int64_t g_stride,
                                                                    const void* w, int w_dtype, void* out,
                                                                    int out_dtype, int I, int group, float eps) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   // one block per (row, group): blockIdx.x = row * (I / group) + group index
   __shared__ float red[kThreads / 32];
   const int ng = I / group;
@@ -156,6 +162,8 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(const void*
                                                                       int E, int topk, float* scores,
                                                                       unsigned int* ticket, int32_t* sel,
                                                                       float* gains) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   // grid: (E, B); scores [B, E] fp32 scratch
   __shared__ float red[kRouterWarps];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -255,13 +263,13 @@ extern "C" int hsd_rms_norm(const void* x, int x_dtype, int64_t x_stride, const 
     const auto* wb = static_cast<const __nv_bfloat16*>(w);
     auto* yb = static_cast<__nv_bfloat16*>(y);
     switch (nv) {
-      case 1: rms_norm_bf16_kernel<1><<<B, kThreads, 0, st>>>(xb, x_stride, wb, yb, D, eps); break;
-      case 2: rms_norm_bf16_kernel<2><<<B, kThreads, 0, st>>>(xb, x_stride, wb, yb, D, eps); break;
-      case 3: rms_norm_bf16_kernel<3><<<B, kThreads, 0, st>>>(xb, x_stride, wb, yb, D, eps); break;
-      default: rms_norm_bf16_kernel<4><<<B, kThreads, 0, st>>>(xb, x_stride, wb, yb, D, eps); break;
+      case 1: hsd::launch_pdl(rms_norm_bf16_kernel<1>, dim3(B), dim3(kThreads), 0, st, xb, x_stride, wb, yb, D, eps); break;
+      case 2: hsd::launch_pdl(rms_norm_bf16_kernel<2>, dim3(B), dim3(kThreads), 0, st, xb, x_stride, wb, yb, D, eps); break;
+      case 3: hsd::launch_pdl(rms_norm_bf16_kernel<3>, dim3(B), dim3(kThreads), 0, st, xb, x_stride, wb, yb, D, eps); break;
+      default: hsd::launch_pdl(rms_norm_bf16_kernel<4>, dim3(B), dim3(kThreads), 0, st, xb, x_stride, wb, yb, D, eps); break;
     }
   } else {
-    rms_norm_kernel<<<B, kThreads, 0, st>>>(x, x_dtype, x_stride, w, w_dtype, y, y_dtype, D, eps);
+    hsd::launch_pdl(rms_norm_kernel, dim3(B), dim3(kThreads), 0, st, x, x_dtype, x_stride, w, w_dtype, y, y_dtype, D, eps);
   }
   return hsd::check_launch("hsd_rms_norm");
 }
@@ -278,7 +286,7 @@ extern "C" int hsd_gated_rms_norm(const void* y, int y_dtype, int64_t y_stride, 
     return hsd::set_error(HSD_ERR_DTYPE, "hsd_gated_rms_norm: bad dtype code");
   const int64_t grid = static_cast<int64_t>(B) * (I / group);
   if (grid > 0x7fffffff) return hsd::set_error(HSD_ERR_SHAPE, "hsd_gated_rms_norm: grid too large");
-  gated_rms_norm_kernel<<<static_cast<unsigned>(grid), kThreads, 0, hsd::as_stream(stream)>>>(
+  hsd::launch_pdl(gated_rms_norm_kernel, dim3(static_cast<unsigned>(grid)), dim3(kThreads), 0, hsd::as_stream(stream),
       y, y_dtype, y_stride, gate, g_dtype, g_stride, w, w_dtype, out, out_dtype, I, group, eps);
   return hsd::check_launch("hsd_gated_rms_norm");
 }
@@ -294,7 +302,7 @@ extern "C" int hsd_router_topk(const void* x, int x_dtype, int64_t x_stride, con
     return hsd::set_error(HSD_ERR_ARG, "hsd_router_topk: null pointer or x_stride < D");
   if (!dtype_ok(x_dtype)) return hsd::set_error(HSD_ERR_DTYPE, "hsd_router_topk: x dtype code %d", x_dtype);
   dim3 grid(E, B);
-  router_topk_kernel<<<grid, kRouterThreads, 0, hsd::as_stream(stream)>>>(x, x_dtype, x_stride, R, B, D, E, topk,
+  hsd::launch_pdl(router_topk_kernel, dim3(grid), dim3(kRouterThreads), 0, hsd::as_stream(stream), x, x_dtype, x_stride, R, B, D, E, topk,
                                                                           scores, ticket, sel, gains);
   return hsd::check_launch("hsd_router_topk");
 }

@@ -97,6 +97,8 @@ __host__ __device__ constexpr int xh_col_stride_u2(int red) { return (red / 16) 
 
 template <int MODE, typename ST>
 __global__ void __launch_bounds__(kThreads) qmma_kernel(const QParams p) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   extern __shared__ __align__(16) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, c = lane & 3;
@@ -395,8 +397,14 @@ __global__ void __launch_bounds__(kSThreads, 1) qstream_kernel(const QParams p, 
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
 
-  if (MODE == kQUp)
+  // programmatic dependent launch: a linear's first weight tiles are requested before the
+  // wait for the previous kernel (weights are never written by the step); the up form's
+  // tiles depend on the routing, so it waits first
+  hsd::pdl_launch_dependents();
+  if (MODE == kQUp) {
+    hsd::pdl_wait();
     for (int i = tid; i < p.B * p.topk; i += kSThreads) sel_s[i] = p.sel[i];
+  }
   if (tid == 0)
     for (int s = 0; s < sc.nst; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8u * s) : "memory");
   __syncthreads();
@@ -418,6 +426,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qstream_kernel(const QParams p, 
       const int t = blockIdx.x + i * gridDim.x;
       if (t < sc.ntiles) issue(t, i);
     }
+  if (MODE != kQUp) hsd::pdl_wait();               // x and y from here on
 
   // ---- the token rows in fp16, permuted for the B fragment, and their fp32 group sums
   const int nch = red / 16;
@@ -572,7 +581,7 @@ int launch_qstream(const QParams& p, const QStreamCfg& sc, size_t smem, cudaStre
     configured = true;
   }
   const int grid = std::min(sc.ntiles, sms);
-  qstream_kernel<MODE, ST><<<grid, kSThreads, smem, st>>>(p, sc);
+  hsd::launch_pdl(qstream_kernel<MODE, ST>, dim3(grid), dim3(kSThreads), smem, st, p, sc);
   return hsd::check_launch(who);
 }
 
@@ -590,7 +599,7 @@ int launch_qmma(const QParams& p, int grid, cudaStream_t st, const char* who) {
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return hsd::check_cuda(e, who);
   }
-  qmma_kernel<MODE, ST><<<grid, kThreads, smem, st>>>(p);
+  hsd::launch_pdl(qmma_kernel<MODE, ST>, dim3(grid), dim3(kThreads), smem, st, p);
   return hsd::check_launch(who);
 }
 

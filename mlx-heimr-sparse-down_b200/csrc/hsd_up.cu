@@ -140,6 +140,8 @@ __device__ __forceinline__ float word_dot(uint32_t w, const float4 a, const floa
 
 template <int MODE, typename ST, int MAXC>
 __global__ void __launch_bounds__(kThreads) moe_qgemv_kernel(const UpParams p, int max_pieces) {
+  hsd::pdl_launch_dependents();   // the next kernel may launch now
+  hsd::pdl_wait();                // inputs of earlier kernels are visible from here
   extern __shared__ __align__(16) float smem_f[];
   float* xs = smem_f;                               // [max_pieces][kPad]
   float* xsum = smem_f + max_pieces * kPad;         // [max_pieces]
@@ -298,7 +300,7 @@ int launch_c(const UpParams& p, int max_pieces, int grid, cudaStream_t st) {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return hsd::check_cuda(e, "qgemv smem attribute");
   }
-  moe_qgemv_kernel<MODE, ST, MAXC><<<grid, kThreads, smem, st>>>(p, max_pieces);
+  hsd::launch_pdl(moe_qgemv_kernel<MODE, ST, MAXC>, dim3(grid), dim3(kThreads), smem, st, p, max_pieces);
   return HSD_OK;
 }
 
