@@ -157,6 +157,9 @@ constexpr int kRouterWarps = kRouterThreads / 32;
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxTopk = 16;
 
+// KP: scores a lane holds in the top-k selection (32 * KP >= E), so the selection's loops
+// cover only the experts there are.
+template <int KP>
 __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(const void* x, int x_dtype, int64_t x_stride,
                                                                       const float* __restrict__ R, int B, int D,
                                                                       int E, int topk, float* scores,
@@ -205,9 +208,9 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(const void*
   if (!last) return;
   __threadfence();
   if (threadIdx.x == 0) *ticket = 0u;
-  // one warp per row: the row's scores into registers once (E <= 1024: 32 per lane), then
-  // k rounds of a warp arg-max over them (ties -> lower id)
-  constexpr int kPer = kMaxExperts / 32;
+  // one warp per row: the row's scores into registers once (KP per lane), then k rounds of a
+  // warp arg-max over them (ties -> lower id)
+  constexpr int kPer = KP;
   for (int row = warp; row < B; row += kRouterWarps) {
     const volatile float* sc = scores + static_cast<int64_t>(row) * E;
     float v[kPer];
@@ -302,7 +305,15 @@ extern "C" int hsd_router_topk(const void* x, int x_dtype, int64_t x_stride, con
     return hsd::set_error(HSD_ERR_ARG, "hsd_router_topk: null pointer or x_stride < D");
   if (!dtype_ok(x_dtype)) return hsd::set_error(HSD_ERR_DTYPE, "hsd_router_topk: x dtype code %d", x_dtype);
   dim3 grid(E, B);
-  hsd::launch_pdl(router_topk_kernel, dim3(grid), dim3(kRouterThreads), 0, hsd::as_stream(stream), x, x_dtype, x_stride, R, B, D, E, topk,
-                                                                          scores, ticket, sel, gains);
+  cudaStream_t st = hsd::as_stream(stream);
+  if (E <= 128)
+    hsd::launch_pdl(router_topk_kernel<4>, grid, dim3(kRouterThreads), 0, st, x, x_dtype, x_stride, R, B, D, E, topk,
+                    scores, ticket, sel, gains);
+  else if (E <= 256)
+    hsd::launch_pdl(router_topk_kernel<8>, grid, dim3(kRouterThreads), 0, st, x, x_dtype, x_stride, R, B, D, E, topk,
+                    scores, ticket, sel, gains);
+  else
+    hsd::launch_pdl(router_topk_kernel<kMaxExperts / 32>, grid, dim3(kRouterThreads), 0, st, x, x_dtype, x_stride, R,
+                    B, D, E, topk, scores, ticket, sel, gains);
   return hsd::check_launch("hsd_router_topk");
 }

@@ -169,7 +169,7 @@ def test_gated_rms_norm_vs_torch(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("B,E,topk", [(1, 128, 6), (3, 128, 6), (4, 16, 4)])
+@pytest.mark.parametrize("B,E,topk", [(1, 128, 6), (3, 128, 6), (4, 16, 4), (2, 256, 8), (1, 1000, 6)])
 def test_router_vs_torch(cuda, B, E, topk):
     from hsd_b200.rowops import Router
     gen = torch.Generator(device=cuda).manual_seed(E + B)
