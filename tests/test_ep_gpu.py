@@ -61,7 +61,7 @@ def _worker(rank, port, q):
 @pytest.mark.gpu
 def test_ep_two_gpus_matches_single_gpu(cuda):
     if torch.cuda.device_count() < WORLD:
-        pytest.skip("needs 2 GPUs (run with gpurun --gpus 2)")
+        pytest.skip("needs 2 GPUs on one machine")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
