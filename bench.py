@@ -10,8 +10,9 @@ the 126 MB L2; the 23 layers' weights are 8.26 GB).
 metric  sparse-down GB/s on NEEDED bytes (live rows x D/2 + live 64-groups x 4D + h + y, the
         reference's byte model, bench/common.py:78-83), headline B = 1, z = 0.90.
 value   needed bytes of all ranks / the max over ranks of the device time of K steps.
-e2e     the same with the step's h / sel / gains copied from pinned host memory and y copied
-        back, inside the timed region.
+e2e     the same with one step's h / sel / gains copied from pinned host memory and the step's
+        y copied back in every timed step, on a copy stream that overlaps them with the compute
+        (inputs of step i+1 go up during step i), joined into the timed region.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 Under torchrun every rank runs its own replica (the decode path does not shard at bs1).
@@ -216,7 +217,7 @@ def max_over_ranks(v, dist_on, device):
     return float(t.item())
 
 
-def timed(fn, steps, warmup, device, dist_on, label="hsd_timed"):
+def timed(fn, steps, warmup, device, dist_on, label="hsd_timed", finish=None):
     """Device time (ms) of `steps` calls of fn(i) after `warmup` calls, CUDA events on the
     current stream, barrier + synchronize on both sides, max over ranks. The timed calls sit
     in an NVTX range named `label` (ncu --nvtx --nvtx-include "<label>/" lists its launches)."""
@@ -232,6 +233,8 @@ def timed(fn, steps, warmup, device, dist_on, label="hsd_timed"):
     e0.record(st)
     for i in range(steps):
         fn(warmup + i)
+    if finish is not None:              # join work fn left on other streams into the region
+        finish()
     e1.record(st)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(device)
@@ -240,18 +243,48 @@ def timed(fn, steps, warmup, device, dist_on, label="hsd_timed"):
 
 
 def e2e_leg(wl, steps, warmup, device, dist_on):
-    """The same steps with each step's inputs copied from pinned host memory and every
-    layer's y copied back, inside the timed region."""
+    """The same steps through host buffers: every timed step copies one step's inputs from
+    pinned host memory and the step's y (every layer's) back to pinned host memory. The
+    copies run on a copy stream, double-buffered the way a serving loop overlaps them: during
+    step i the inputs of step i+1 go up (its own input set, so no step reads a buffer being
+    written), then y of step i comes down once step i is done; step i+1 waits for its inputs.
+    The copy stream is joined into the timed region before its end event."""
     host_in = [buf.cpu().pin_memory() for (buf, _) in wl.sets]
     host_out = [torch.empty(y.shape, dtype=y.dtype).pin_memory() for y in wl.ys]
+    comp = torch.cuda.current_stream(device)
+    copy = torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(N_SETS)]
+    ev_done = [torch.cuda.Event() for _ in range(N_SETS)]
+    ev_out = [torch.cuda.Event() for _ in range(N_SETS)]
+
+    def upload(si):
+        copy.wait_event(ev_done[si])                 # the set's previous step is finished
+        with torch.cuda.stream(copy):
+            wl.sets[si][0].copy_(host_in[si], non_blocking=True)
+        ev_in[si].record(copy)
+
+    for si in range(N_SETS):                        # every set computed once before: events valid
+        ev_done[si].record(comp)
+        ev_out[si].record(copy)
+    upload(0)
 
     def fn(i):
-        si = i % N_SETS
-        wl.sets[si][0].copy_(host_in[si], non_blocking=True)
+        si, sj = i % N_SETS, (i + 1) % N_SETS
+        comp.wait_event(ev_in[si])                   # this step's inputs are up
+        comp.wait_event(ev_out[si])                  # y of the set's previous step is down
         wl.graphs[si].replay()
-        host_out[si].copy_(wl.ys[si], non_blocking=True)
+        ev_done[si].record(comp)
+        upload(sj)                                   # the next step's inputs, during this step
+        copy.wait_event(ev_done[si])
+        with torch.cuda.stream(copy):
+            host_out[si].copy_(wl.ys[si], non_blocking=True)
+        ev_out[si].record(copy)
 
-    ms = timed(fn, steps, warmup, device, dist_on)
+    def finish():
+        comp.wait_stream(copy)
+
+    ms = timed(fn, steps, warmup, device, dist_on, finish=finish)
+    torch.cuda.synchronize(device)
     h2d = host_in[0].numel()
     d2h = host_out[0].numel() * host_out[0].element_size()
     return ms, h2d, d2h
@@ -548,7 +581,9 @@ def main():
                          f"{N_SETS * wl.bytes_per_step / 1e9:.2f} GB > 126 MB L2); weights 8.26 GB",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "needed_MB_per_step": wl.bytes_per_step / 1e6},
-        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "copies": "pinned host buffers on a copy stream: inputs of step i+1 up during step i, "
+                          "y of step i down after it; the copy stream is joined before the end event"},
         "gpu_launches": steps * N_LAYERS,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
