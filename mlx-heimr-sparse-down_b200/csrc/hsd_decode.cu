@@ -18,14 +18,18 @@
 //   1. one 16-byte load per thread brings the batch's h columns (and each group's expert
 //      id and gain) into shared memory;
 //   2. each warp builds its groups' live masks with two ballots and, for a live group,
-//      starts the TMA bulk copies of the group's scale and bias chunks (C*2 bytes each);
+//      starts the copies of the group's scale and bias chunks (C*2 bytes each) as 16-byte
+//      cp.async pieces, one per lane;
 //   3. every warp scans the live counts, cuts the live rows into sub-batches of whole groups
 //      of at most SBR rows, and compacts its groups' live rows into an ascending list
 //      (ballot prefix popcounts); each lane holding a live row of one of the first `slots`
-//      sub-batches starts the TMA bulk copy of that row's C/2-byte chunk into the
-//      sub-batch's slot of the shared-memory ring. A slot's copies complete on the slot's
-//      mbarrier, whose single arrival carries the sub-batch's byte count, so up to `slots`
-//      sub-batches are in flight at once and a copy costs one instruction;
+//      sub-batches starts the copy of that row's C/2-byte chunk into the sub-batch's slot of
+//      the shared-memory ring as one TMA bulk copy. The TMA unit takes one bulk copy about
+//      every 16 cycles, which makes the issue of the ~200 row copies per CTA the longest
+//      phase of a token's chain; the scale/bias pieces of step 2 go over the load/store
+//      path, beside it, instead of adding ~60 bulk copies to that queue. A slot's copies
+//      complete on the slot's mbarrier: one arrival carries the sub-batch's TMA bytes, and
+//      every thread adds one arrival that fires when its own cp.async pieces have landed;
 //   4. per sub-batch, as its slot's mbarrier completes: thread (word wp, group lane gl)
 //      walks the live rows of its groups gl, gl+NGL, ... of the sub-batch in shared memory,
 //      accumulating acc'[n] = sum h * (1 + q_n/16) and hsum = sum h in fp32, and folds each
@@ -192,6 +196,18 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
 }
 
+// 16 bytes global -> this CTA's shared memory on the load/store path (cp.async, L2 hint),
+// beside the TMA unit: the two paths issue in parallel.
+__device__ __forceinline__ void cp16(void* dst, const void* src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;"
+               ::"r"(smem_u32(dst)), "l"(src), "l"(pol) : "memory");
+}
+// One arrival on `bar` once every cp.async this thread issued before it has landed (the
+// barrier's expected count includes one such arrival per thread).
+__device__ __forceinline__ void cp_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // ---- distributed shared memory helpers
 // The address of this CTA's shared-memory location `a` in cluster CTA `r`.
 __device__ __forceinline__ uint32_t mapa_u32(uint32_t a, uint32_t r) {
@@ -248,14 +264,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
   const int SBR = p.SBR, nring = p.nring;
   const uint32_t bar0 = smem_u32(&S.bars[0]);     // slot k's mbarrier: bar0 + 8*k
   const uint32_t rbar = smem_u32(&S.rbar);
-  const uint32_t meta_bytes = static_cast<uint32_t>(nwc) * 16;   // 8 outputs x 2 bytes per word
   const uint32_t row_bytes = static_cast<uint32_t>(nwc) * 4;
   constexpr int per = C / kCluster;               // outputs of the chunk each CTA finishes
   uint32_t phases = 0;                            // bit k: the parity slot k waits for next
   const uint64_t pol = evict_first_policy();
 
   if (tid == 0) {
-    for (int k = 0; k < kMaxSlots; ++k) mbar_init(bar0 + 8u * k, 1);
+    // a slot's phase: the arrival carrying its TMA bytes + one cp.async arrival per thread
+    for (int k = 0; k < kMaxSlots; ++k) mbar_init(bar0 + 8u * k, 1 + THREADS);
     mbar_init(rbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // the 8 slices of C/8 partials that the cluster's CTAs push here complete this phase
@@ -323,12 +339,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
         S.gmask[gi] = m;
         S.gcnt[gi] = __popcll(m);
       }
-      if (m != 0ull && p.loadsc && lane < 2) {   // a live group's scale (lane 0) / bias (lane 1) chunk
+      if (m != 0ull && p.loadsc && lane < nwc) {   // a live group's scale and bias chunks: 16 bytes a lane
         const int src = S.gsrc[gi];
         const int64_t grow = (src >= 0) ? static_cast<int64_t>(src) * GF + S.gloc[gi] : S.gloc[gi];
-        const uint16_t* base = (src >= 0) ? (lane ? p.pb : p.ps) : (lane ? p.spb : p.sps);
-        bulk_g2s((lane ? S.meta_b : S.meta_s) + gi * C, base + grow * p.D + static_cast<int64_t>(w0) * 8,
-                 meta_bytes, bar0, pol);                 // with sub-batch 0, on slot 0
+        const int64_t go = grow * p.D + static_cast<int64_t>(w0) * 8 + lane * 8;
+        cp16(S.meta_s + gi * C + lane * 8, ((src >= 0) ? p.ps : p.sps) + go, pol);   // complete on slot 0
+        cp16(S.meta_b + gi * C + lane * 8, ((src >= 0) ? p.pb : p.spb) + go, pol);
       }
     }
     __syncthreads();
@@ -366,14 +382,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
         if (lane == 0) S.goff[ng] = nrows;
         if (lane < nsb) S.sbeg[lane] = my_sbeg;
         if (lane == 0) S.sbeg[nsb] = nrows;
-        // each in-flight sub-batch's byte count, registered once with its slot's single
-        // arrival (copies already issued may complete first: the phase cannot end before
-        // the arrival); slot 0 also carries the batch's scale/bias chunks
-        const unsigned live_groups = __popc(__ballot_sync(0xffffffffu, c > 0));
+        // each in-flight sub-batch's TMA byte count (its rows), registered once with its
+        // slot's arrival (copies already issued may complete first: the phase cannot end
+        // before the arrivals); the cp.async scale/bias chunks complete on slot 0 through
+        // the threads' cp.async arrivals
         if (lane < min(nsb, nring))
-          mbar_arrive_expect_tx(bar0 + 8u * lane,
-                                static_cast<uint32_t>(my_send - my_sbeg) * row_bytes +
-                                    ((lane == 0 && p.loadsc) ? live_groups * 2u * meta_bytes : 0u));
+          mbar_arrive_expect_tx(bar0 + 8u * lane, static_cast<uint32_t>(my_send - my_sbeg) * row_bytes);
       }
       for (int gi = warp; gi < ng; gi += WARPS) {
         const unsigned long long m = S.gmask[gi];
@@ -391,12 +405,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
             const int idx = base + live_prefix(m, j);
             S.rows[idx] = static_cast<uint16_t>((gi << 6) | j);
             S.hrow[idx] = S.hs[gi * kGS + j];
-            if (sb < nring)
-              bulk_g2s(ring + static_cast<size_t>(sb * SBR + idx - sb_first) * NWC, wbase + (rowbase + j) * p.NW + w0,
-                       row_bytes, bar0 + 8u * sb, pol);
+            if (sb < nring) {
+              uint32_t* dst = ring + static_cast<size_t>(sb * SBR + idx - sb_first) * NWC;
+              const uint32_t* src = wbase + (rowbase + j) * p.NW + w0;
+              bulk_g2s(dst, src, row_bytes, bar0 + 8u * sb, pol);
+            }
           }
         }
       }
+      // one cp.async arrival per thread on every slot in flight (the scale/bias pieces land
+      // with slot 0's phase)
+      for (int k = 0; k < min(nsb, nring); ++k) cp_arrive(bar0 + 8u * k);
     }
     __syncthreads();
 
@@ -462,8 +481,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
           const int64_t neuron = static_cast<int64_t>(S.gloc[gi]) * kGS + j;
           const uint32_t* g = (src >= 0) ? p.pw + (static_cast<int64_t>(src) * p.F + neuron) * p.NW
                                          : p.spw + neuron * p.NW;
-          bulk_g2s(ring + (static_cast<size_t>(sk) * SBR + r) * NWC, g + w0, row_bytes, bk, pol);
+          uint32_t* dst = ring + (static_cast<size_t>(sk) * SBR + r) * NWC;
+          bulk_g2s(dst, g + w0, row_bytes, bk, pol);
         }
+        cp_arrive(bk);
       }
     }
     __syncthreads();                             // the ring, meta and hs are rewritten next
