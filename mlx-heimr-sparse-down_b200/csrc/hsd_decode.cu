@@ -148,6 +148,14 @@ __device__ __forceinline__ float nib_unit(uint32_t q) {
   return __uint_as_float((m & 0x00780000u) | 0x3F800000u);
 }
 
+// (x, y) = (fma(h, u, x), fma(h, v, y)), each rounded to nearest as fmaf does: one packed
+// fp32 FMA (fma.rn.f32x2, sm_100) in place of two, the same bits
+__device__ __forceinline__ void ffma2(float& x, float& y, float h, float u, float v) {
+  asm("{\n .reg .b64 a, b, c;\n mov.b64 a, {%2, %2};\n mov.b64 b, {%3, %4};\n mov.b64 c, {%0, %1};\n"
+      " fma.rn.f32x2 c, a, b, c;\n mov.b64 {%0, %1}, c;\n}"
+      : "+f"(x), "+f"(y) : "f"(h), "f"(u), "f"(v));
+}
+
 template <typename HT>
 __device__ __forceinline__ float load_h(const void* h, int64_t idx) {
   return hsd::to_f32<HT>(reinterpret_cast<const HT*>(h)[idx]);
@@ -442,14 +450,10 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
             const float hv = S.hrow[r];
             const uint32_t q = stage[(r - r0) * NWC + wp];
             hsum += hv;
-            acc[0] = fmaf(hv, nib_unit<0>(q), acc[0]);
-            acc[1] = fmaf(hv, nib_unit<1>(q), acc[1]);
-            acc[2] = fmaf(hv, nib_unit<2>(q), acc[2]);
-            acc[3] = fmaf(hv, nib_unit<3>(q), acc[3]);
-            acc[4] = fmaf(hv, nib_unit<4>(q), acc[4]);
-            acc[5] = fmaf(hv, nib_unit<5>(q), acc[5]);
-            acc[6] = fmaf(hv, nib_unit<6>(q), acc[6]);
-            acc[7] = fmaf(hv, nib_unit<7>(q), acc[7]);
+            ffma2(acc[0], acc[1], hv, nib_unit<0>(q), nib_unit<1>(q));
+            ffma2(acc[2], acc[3], hv, nib_unit<2>(q), nib_unit<3>(q));
+            ffma2(acc[4], acc[5], hv, nib_unit<4>(q), nib_unit<5>(q));
+            ffma2(acc[6], acc[7], hv, nib_unit<6>(q), nib_unit<7>(q));
           }
           const float g = S.ggain[gi];
           if (p.loadsc) {
