@@ -15,7 +15,14 @@ e2e     the same with one step's h / sel / gains copied from pinned host memory 
         (inputs of step i+1 go up during step i), joined into the timed region.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-Under torchrun every rank runs its own replica (the decode path does not shard at bs1).
+Under torchrun every rank runs its own replica (the decode path does not shard at bs1), and
+the expert-parallel legs (batch decode, prefill) shard the experts over the ranks.
+
+--impl reference times the reference's decode algorithm on the host cores (the C port in
+oracle/, all 23 layers, the same seeded weights and input sets). That arm never imports the
+hsd_b200 package and never loads libhsd.so: its weights are drawn on the GPU by the same
+seeded torch calls (synth.py loaded by file path) and permuted to neuron-major on the host by
+the oracle's C transpose.
 """
 import argparse
 import json
@@ -28,11 +35,29 @@ import time
 import torch
 
 REPO = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.path.join(REPO, "mlx-heimr-sparse-down_b200"))
+PKG_ROOT = os.path.join(REPO, "mlx-heimr-sparse-down_b200")
 sys.path.insert(0, REPO)
 
-import hsd_b200  # noqa: E402
-from hsd_b200 import synth  # noqa: E402
+
+def _load_synth():
+    """The seeded input generator (plain torch), loaded by file path so that the reference arm
+    never imports the hsd_b200 package (whose import loads libhsd.so)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("hsd_synth", os.path.join(PKG_ROOT, "hsd_b200", "synth.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _hsd():
+    """The product package (this repository's arm only)."""
+    if PKG_ROOT not in sys.path:
+        sys.path.insert(0, PKG_ROOT)
+    import hsd_b200
+    return hsd_b200
+
+
+synth = _load_synth()
 
 D, F, FS, E, TOPK = synth.D_REF, synth.F_REF, synth.FS_REF, synth.E_REF, synth.TOPK_REF
 N_LAYERS = 23      # MoE layers of the decode path (config 1); --layers lowers it for profiling
@@ -125,6 +150,7 @@ def needed_bytes(h, sel, y_bytes=2):
 def make_layers(device, seed=1000):
     """23 layers of routed + shared down projections, generated in the checkpoint layout
     and permuted to neuron-major by the layout kernels."""
+    hsd_b200 = _hsd()
     layers = []
     for l in range(N_LAYERS):
         gen = torch.Generator(device=device).manual_seed(seed + l)
@@ -177,6 +203,7 @@ class DecodeWorkload:
         self.graphs = None
 
     def run_set(self, si):
+        hsd_b200 = _hsd()
         _, views = self.sets[si]
         y = self.ys[si]
         for l, (h, sel, gains) in enumerate(views):
@@ -290,46 +317,82 @@ def e2e_leg(wl, steps, warmup, device, dist_on):
     return ms, h2d, d2h
 
 
-def cpu_leg(layers, wl, budget_s=10.0, n_layers=4):
-    """The reference's decode algorithm (the C port in oracle/, OpenMP over all host
-    threads) on a bounded sample: the first n_layers layers, the workload's rotating input
-    sets, repeated until ~budget_s seconds. -> (GB/s on needed bytes, cores, sample)."""
+def _np_u32(t):
+    import numpy as np
+    return t.cpu().contiguous().view(torch.int32).numpy().view(np.uint32)
+
+
+def _np_u16(t):
+    import numpy as np
+    return t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def host_layers_from_device(layers):
+    """This arm's neuron-major layers (built by libhsd's transpose) copied to the host."""
+    return [tuple((_np_u32 if t.dtype == torch.int32 else _np_u16)(t) for t in lay) for lay in layers]
+
+
+def host_layers_oracle(device, seed=1000):
+    """The same N_LAYERS layers as make_layers, without libhsd: the same seeded generator calls
+    draw the checkpoint-layout weights on the device, and the oracle permutes them to
+    neuron-major on the host (its C nibble transpose; scales / biases swap their last two axes).
+    The result is bit-identical to make_layers' layout."""
     import numpy as np
     from oracle import cport
+    out = []
+    for l in range(N_LAYERS):
+        gen = torch.Generator(device=device).manual_seed(seed + l)
+        w, s, b = synth.quantized_weights((E, D, F), gen, device)
+        sw, ss, sb = synth.quantized_weights((D, FS), gen, device)
+        swap = lambda t: np.ascontiguousarray(np.swapaxes(_np_u16(t), -1, -2))  # noqa: E731
+        out.append((cport.nibble_transpose(_np_u32(w)), swap(s), swap(b),
+                    cport.nibble_transpose(_np_u32(sw)), swap(ss), swap(sb)))
+        del w, s, b, sw, ss, sb
+    return out
+
+
+def host_inputs(sets):
+    """make_inputs' sets on the host: per set, per layer (h f32, sel, gains, needed bytes)."""
+    return [[(h.float().cpu().numpy(), sel.cpu().numpy(), gains.cpu().numpy(), needed_bytes(h, sel))
+             for (h, sel, gains) in views] for (_, views) in sets]
+
+
+def cpu_steps(host, ins, steps, warmup=1, budget_s=None):
+    """Decode steps of the reference's algorithm on the host (the C port in oracle/, OpenMP over
+    every host thread): one step = the N_LAYERS layers with one rotating input set, exactly the
+    GPU arm's step. Runs `steps` steps after `warmup`, or, with budget_s, as many as fit.
+    -> (GB/s on needed bytes, ms per step, cores, steps run)."""
+    from oracle import cport
     cores = os.cpu_count() or 1
-    host = []
-    for l in range(n_layers):
-        pw, ps, pb, spw, sps, spb = layers[l]
-        host.append(tuple(t.cpu().contiguous().view(torch.int32 if t.dtype == torch.int32 else torch.int16)
-                          .numpy().view(np.uint32 if t.dtype == torch.int32 else np.uint16)
-                          for t in (pw, ps, pb, spw, sps, spb)))
-    ins = []
-    for si in range(N_SETS):
-        _, views = wl.sets[si]
-        for l in range(n_layers):
-            h, sel, gains = views[l]
-            ins.append((l, h.float().cpu().numpy(), sel.cpu().numpy(), gains.cpu().numpy(),
-                        needed_bytes(h, sel)))
-    # warm-up (page in)
-    l, h, sel, gains, _ = ins[0]
-    cport.sparse_down(h, sel, gains, *host[l], F=F, FS=FS, D=D, topk=TOPK, nthreads=cores)
-    t0 = time.perf_counter()
-    nbytes, calls = 0, 0
-    while time.perf_counter() - t0 < budget_s:
-        for (l, h, sel, gains, nb) in ins:
+
+    def step(i):
+        nb = 0
+        for l, (h, sel, gains, n) in enumerate(ins[i % len(ins)]):
             cport.sparse_down(h, sel, gains, *host[l], F=F, FS=FS, D=D, topk=TOPK, nthreads=cores)
-            nbytes += nb
-            calls += 1
+            nb += n
+        return nb
+
+    for i in range(warmup):
+        step(i)
+    t0 = time.perf_counter()
+    nbytes, n = 0, 0
+    while (budget_s is None and n < steps) or (budget_s is not None and time.perf_counter() - t0 < budget_s):
+        nbytes += step(warmup + n)
+        n += 1
     dt = time.perf_counter() - t0
-    sample = (f"layers 0-{n_layers - 1} of {N_LAYERS}, B={wl.B}, z={wl.z:.2f}, {N_SETS} rotating input sets, "
-              f"{calls} calls in {dt:.1f} s (C port of the reference kernel's algorithm, OpenMP)")
-    return nbytes / dt / 1e9, cores, sample
+    return nbytes / dt / 1e9, 1e3 * dt / n, cores, n
 
 
 def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512):
     """Config 2: T tokens in chunks of `chunk` through one MoE layer (layer 0), Zipf(1.1)
     routing, h = relu(N(-1.28, 1))^2. Times tile order + gather + tcgen05 GEMM + reduce per
-    chunk (CUDA events, max over ranks) -> dict with tensor-pipe and byte rates."""
+    chunk (CUDA events, max over ranks) -> dict with tensor-pipe and byte rates.
+
+    FLOPs: dense-equivalent 2*T*(6F+FS)*D (the headline tensor fraction, against the measured
+    bf16 peak); useful 2*D*sum over tiles of n_valid_slots * U_tile (the reference's union GEMM
+    work, U the tile's union of live rows); executed = what the MMAs run (128-slot tiles
+    including padding, every K-group the kernel does not skip)."""
+    hsd_b200 = _hsd()
     from hsd_b200 import prefill as hp
     gen = torch.Generator(device=device).manual_seed(77)
     sel, sc = synth.route_zipf(T, E, TOPK, gen, device)
@@ -346,34 +409,45 @@ def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512):
                                    out=y[a:b], workspace=ws)
 
     ms = timed(run, reps, 3, device, dist_on) / reps
-    # executed MMA work: every non-empty tile is 128 slots x its K x D
-    ex = 0
+    ex, useful, kgroups_live, kgroups_all = 0.0, 0.0, 0, 0
     for a, b in chunks:
-        te, _ = hp.build_tiles(sel[a:b].contiguous(), E, hp.GEMM_TT)
-        te = te.cpu()
-        n_routed = int(((te >= 0) & (te < E)).sum())
-        n_shared = int((te == E).sum())
-        ex += 2.0 * hp.GEMM_TT * D * (n_routed * F + n_shared * FS)
+        te, ts = hp.build_tiles(sel[a:b].contiguous(), E, hp.GEMM_TT)
+        _, uc = hp.build_union(h[a:b].contiguous(), te, ts, F=F, FS=FS, topk=TOPK, E=E, tt=hp.GEMM_TT)
+        te, ts, uc = te.cpu(), ts.view(-1, hp.GEMM_TT).cpu(), uc.cpu()
+        nvalid = (ts >= 0).sum(1)
+        nonempty = te >= 0
+        kk = torch.where(te == E, FS, F)
+        ex += float(2.0 * hp.GEMM_TT * D * (kk[nonempty]).sum())
+        useful += float(2.0 * D * (nvalid[nonempty] * uc[nonempty]).sum())
     dense = 2.0 * T * (TOPK * F + FS) * D
     peak_t = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["bf16_tflops"] \
         if os.path.exists(os.path.join(REPO, "MEASURED_PEAKS.json")) else 1590.0
     wbytes = len(chunks) * (E * F * D // 2 + E * (F // 64) * D * 4 + FS * D // 2 + (FS // 64) * D * 4)
+    s = ms / 1e3
     return {"workload": f"config2: {T} tokens in chunks of {chunk}, one MoE layer, Zipf(1.1) top-6, z=0.90",
-            "ms": ms, "tokens_per_s": T / (ms / 1e3),
-            "dense_equiv_tflops": dense / (ms / 1e3) / 1e12,
-            "executed_mma_tflops": ex / (ms / 1e3) / 1e12,
-            "tensor_frac_of_measured_bf16": ex / (ms / 1e3) / 1e12 / peak_t,
-            "weight_GBps": wbytes / (ms / 1e3) / 1e9,
-            "note": "executed = 128-slot tiles incl. padding (fp16 operands, fp32 accumulate); "
-                    "dense_equiv = 2*T*(6F+FS)*D"}
+            "ms": ms, "tokens_per_s": T / s,
+            "dense_equiv_tflops": dense / s / 1e12,
+            "tensor_frac": dense / s / 1e12 / peak_t,
+            "useful_tflops": useful / s / 1e12,
+            "useful_frac": useful / s / 1e12 / peak_t,
+            "executed_mma_tflops": ex / s / 1e12,
+            "executed_frac": ex / s / 1e12 / peak_t,
+            "peak_tflops": peak_t,
+            "weight_GBps": wbytes / s / 1e9,
+            "note": "tensor_frac = dense-equivalent 2*T*(6F+FS)*D per second over the measured bf16 burst peak; "
+                    "useful = 2*D*sum(n_valid*U) over tiles (the reference's union GEMM); executed = 128-slot "
+                    "tiles incl. padding x every K-group (fp16 operands, fp32 accumulate)"}
 
 
 def ep_leg(layers, device, dist_on, reps=10):
     """Expert-parallel MoE down projection across the ranks (layer 0's experts sharded E/G per
     GPU, tokens on their home rank): batch decode B = 64 and a prefill chunk of 512 tokens per
     rank (weak scaling), NCCL all-to-all dispatch / combine around this library's kernels.
-    -> dict of tokens/s summed over ranks (device time, max over ranks)."""
+    Every leg is checked against the single-GPU operator on the same tokens with all 128
+    experts resident (rel_err = max|ep - single| / max|single|, bar 5e-3).
+    -> dict of tokens/s summed over ranks (device time, max over ranks) and the parity."""
     import torch.distributed as dist
+    hsd_b200 = _hsd()
     from hsd_b200.ep import ExpertParallelDown
     world, rank = dist.get_world_size(), dist.get_rank()
     EL = E // world
@@ -381,31 +455,141 @@ def ep_leg(layers, device, dist_on, reps=10):
     ep = ExpertParallelDown(E, F, FS, D, TOPK, pw[rank * EL:(rank + 1) * EL].contiguous(),
                             ps[rank * EL:(rank + 1) * EL].contiguous(), pb[rank * EL:(rank + 1) * EL].contiguous(),
                             spw, sps, spb)
-    out = {}
+    out, worst = {}, 0.0
     for name, T in (("batch_decode_B64", 64), ("prefill_chunk_512", 512)):
         gen = torch.Generator(device=device).manual_seed(100 + rank)
         sel, sc = synth.route_zipf(T, E, TOPK, gen, device)
         gains = torch.cat([sc, torch.ones((T, 1), device=device)], 1).contiguous()
         h = synth.relu2_activations((T, TOPK * F + FS), 0.90, gen, device)
         ms = timed(lambda _: ep(h, sel, gains), reps, 3, device, dist_on) / reps
-        out[name] = {"ms": ms, "tokens_per_s_all_ranks": world * T / (ms / 1e3)}
+        y_ep = ep(h, sel, gains)
+        if T <= 8 * 8:
+            y_one = hsd_b200.sparse_down(h, sel, gains, *layers[0], F=F, FS=FS, D=D, topk=TOPK,
+                                         out_dtype=torch.float32)
+        else:
+            y_one = hsd_b200.sparse_down_prefill(h, sel, gains, *layers[0], F=F, FS=FS, D=D, topk=TOPK, E=E,
+                                                 out_dtype=torch.float32)
+        err = float((y_ep - y_one).abs().max() / y_one.abs().max().clamp_min(1e-30))
+        errs = torch.tensor([err], dtype=torch.float64, device=device)
+        dist.all_reduce(errs, op=dist.ReduceOp.MAX)
+        worst = max(worst, float(errs.item()))
+        out[name] = {"ms": ms, "tokens_per_s_all_ranks": world * T / (ms / 1e3), "rel_err": float(errs.item())}
     out["gpus"] = world
-    out["note"] = "experts 0..127 split 128/G per GPU; slots exchanged with NCCL all_to_all_single"
+    out["parity_ok"] = worst < 5e-3
+    out["note"] = ("experts 0..127 split 128/G per GPU; slots exchanged with NCCL all_to_all_single; rel_err = "
+                   "max over ranks of max|ep - single-GPU operator| / max|single| on the same tokens")
     return out
 
 
+def mamba_leg(device, reps=50, n_layers=23, ks=(2, 3)):
+    """Config 3: MTP verify + rollback on the Mamba-2 layers (64 heads x 64, state 128, 8 groups,
+    conv 4; 4-bit in / out projections). One step = a verify of 1+k rows through each of the
+    model's n_layers Mamba-2 blocks on their resident buffers (state 2 MiB per row per layer,
+    n_layers blocks rotate the L2), then the rollback to an accepted prefix drawn from 0..k.
+    Reports us per layer for the whole block, for the scan kernel alone (with GB/s on its
+    state traffic: the 2 MiB state read + 1+k per-row 2 MiB checkpoints written), and for the
+    rollback: one device int on the resident buffers, or the copying form
+    (hsd_mamba_rollback: 2 MiB state + conv window) with its GB/s."""
+    _hsd()
+    from hsd_b200 import mamba as hm
+    blocks = [hm.random_mamba2(300 + l, device=device) for l in range(n_layers)]
+    b0 = blocks[0]
+    state_b = b0.H * b0.P * b0.N * 4
+    res = {"workload": f"config3: {n_layers} Mamba-2 blocks (H={b0.H} P={b0.P} N={b0.N} G={b0.G} K={b0.K}), "
+                       "verify 1+k rows then roll back to 1+a rows, a ~ U{0..k}",
+           "state_MiB_per_row": state_b / 2 ** 20}
+    for k in ks:
+        L = 1 + k
+        gen = torch.Generator(device=device).manual_seed(500 + k)
+        rcs = [hm.ResidentMambaCache(b, rows=L, device=device) for b in blocks]
+        for rc in rcs:
+            rc.states.normal_(0, 0.1, generator=gen)
+        xs = [torch.randn((L, 2688), generator=gen, device=device).to(torch.bfloat16) for _ in range(4)]
+        keep = torch.randint(1, L + 1, (64,), generator=gen, device=device, dtype=torch.int32)
+        n_keep = torch.ones(1, dtype=torch.int32, device=device)
+        step_i = torch.zeros(1, dtype=torch.int64, device=device)
+        xin = torch.empty((L, 2688), dtype=torch.bfloat16, device=device)
+
+        def body(xin=xin, rcs=rcs, n_keep=n_keep, keep=keep, step_i=step_i):
+            x = xin
+            for b, rc in zip(blocks, rcs):
+                x = hm.mamba_step_resident(b, x, rc, n_keep)
+            n_keep.copy_(keep.index_select(0, step_i % keep.shape[0]))   # the rollback: one device int
+            step_i.add_(1)
+            return x
+
+        def scan_body(rcs=rcs, n_keep=n_keep):
+            for b, rc in zip(blocks, rcs):
+                hm.ssm_step(sc_in[0], sc_in[1], b.A_log, b.D, b.dt_bias, rc.states, n_keep, H=b.H, P=b.P,
+                            G=b.G, N=b.N)
+
+        sc_in = (torch.randn((L, b0.conv_dim), generator=gen, device=device).to(torch.bfloat16),
+                 (torch.randn((L, b0.H), generator=gen, device=device) * 0.5).to(torch.bfloat16))
+        graphs = {}
+        for name, fn in (("block", body), ("scan", scan_body)):
+            st = torch.cuda.Stream(device)
+            st.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(st):
+                xin.copy_(xs[0])
+                fn()
+            torch.cuda.current_stream(device).wait_stream(st)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            graphs[name] = g
+
+        def run_block(i):
+            xin.copy_(xs[i % len(xs)])
+            graphs["block"].replay()
+
+        ms_block = timed(run_block, reps, 3, device, False, label="hsd_mamba") / reps
+        ms_scan = timed(lambda _: graphs["scan"].replay(), reps, 3, device, False, label="hsd_mamba") / reps
+        # the copying rollback (callers that keep their cache tensors at fixed addresses)
+        conv_out = torch.empty((b0.K - 1, b0.conv_dim), dtype=torch.bfloat16, device=device)
+        state_out = torch.empty((b0.H, b0.P, b0.N), dtype=torch.float32, device=device)
+
+        def rb(i):
+            for rc in rcs:
+                hm.rollback_into(rc.padded, rc.states, 1 + (i % L), conv_out, state_out)
+
+        ms_rb = timed(rb, reps, 3, device, False, label="hsd_mamba") / reps
+        scan_bytes = state_b * (1 + L) + L * (b0.conv_dim + b0.H) * 2 + L * b0.I * 4
+        rb_bytes = 2 * state_b + 2 * (b0.K - 1) * b0.conv_dim * 2
+        res[f"k{k}"] = {"rows": L,
+                        "verify_us_per_layer": 1e3 * ms_block / n_layers,
+                        "scan_us_per_layer": 1e3 * ms_scan / n_layers,
+                        "scan_GBps": scan_bytes * n_layers / (ms_scan / 1e3) / 1e9,
+                        "rollback_resident_us": "one device int32 write inside the verify graph",
+                        "rollback_copy_us_per_layer": 1e3 * ms_rb / n_layers,
+                        "rollback_copy_GBps": rb_bytes * n_layers / (ms_rb / 1e3) / 1e9}
+        del graphs, rcs
+    del blocks
+    torch.cuda.empty_cache()
+    return res
+
+
 def traffic_from_profile():
-    """Per-launch DRAM traffic of the decode kernel from the committed ncu summary."""
+    """Per-launch DRAM traffic of the decode kernel (dram__bytes_read.sum + write.sum, one ncu
+    capture) from the committed summary -- only when that summary was taken of the decode
+    kernel's current source (its sha256 prefix is recorded there), else None."""
+    import hashlib
     p = os.path.join(REPO, "profiles", "decode_sparse_down_ncu.md")
-    if not os.path.exists(p):
-        return None
+    src = os.path.join(PKG_ROOT, "csrc", "hsd_decode.cu")
+    if not os.path.exists(p) or not os.path.exists(src):
+        return None, "no profile"
+    sha = hashlib.sha256(open(src, "rb").read()).hexdigest()[:16]
+    traffic, prof_sha = None, None
     for line in open(p):
         if line.startswith("traffic_bytes_per_launch:"):
             try:
-                return float(line.split(":", 1)[1].split()[0])
+                traffic = float(line.split(":", 1)[1].split()[0])
             except ValueError:
-                return None
-    return None
+                traffic = None
+        if line.startswith("source_sha256_16:"):
+            prof_sha = line.split(":", 1)[1].strip()
+    if prof_sha != sha:
+        return None, f"profile of another kernel source ({prof_sha} vs {sha})"
+    return traffic, f"ncu capture of csrc/hsd_decode.cu sha256 {sha} (profiles/decode_sparse_down_ncu.md)"
 
 
 def model_leg(device, n_tokens=256, prompt_len=128):
@@ -413,6 +597,7 @@ def model_leg(device, n_tokens=256, prompt_len=128):
     prompt, then n_tokens tokens in each mode (a captured CUDA graph per decode step or per
     MTP iteration). tok/s counts the generated tokens after the first over the decode time
     (host-timed, as the reference's loop reports it); the token lists are compared exactly."""
+    _hsd()
     from hsd_b200.model import ModelArgs, MTPHead, NemotronModel, identical_prefix
     t0 = time.time()
     m = NemotronModel(ModelArgs(), seed=0, device=device, mode="dense")
@@ -471,6 +656,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--only-prefill", action="store_true", help="profiling: the prefill leg alone")
     ap.add_argument("--no-model", action="store_true", help="skip the config-4 model leg")
+    ap.add_argument("--no-mamba", action="store_true", help="skip the config-3 Mamba verify / rollback leg")
     ap.add_argument("--model-tokens", type=int, default=256)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--layers", type=int, default=23, help="fewer layers: small profiling case only")
@@ -499,22 +685,29 @@ def main():
                 import torch.distributed as dist
                 dist.destroy_process_group()
             return
-        layers = make_layers(device)
-        wl = DecodeWorkload(layers, 1, 0.90, device, seed=1)
-        # one warm-up sample, then `steps` timed samples of ~1 s each (bounded)
-        per = max(1.0, min(10.0, 60.0 / (steps + warmup)))
-        cpu_leg(layers, wl, budget_s=min(2.0, per))
-        vals = [cpu_leg(layers, wl, budget_s=per) for _ in range(steps)]
-        v = sum(x[0] for x in vals) / len(vals)
+        t0 = time.perf_counter()
+        host = host_layers_oracle(device)
+        sets = make_inputs(1, 0.90, device, seed=1)          # the GPU arm's input sets (same seeds)
+        ins = host_inputs(sets)
+        build_s = time.perf_counter() - t0
+        v, ms_step, cores, n = cpu_steps(host, ins, steps, warmup=min(warmup, 3))
         line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
-                "steps": steps, "warmup": warmup, "ms_per_step": None, "higher_is_better": True,
+                "steps": n, "warmup": min(warmup, 3), "ms_per_step": ms_step, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16 h, u4 weights, f32 accumulate",
-                "data": "synthetic", "config": {"workload": "config1: 23 MoE decode layers, B=1, z=0.90 (CPU sample)"},
-                "cpu_baseline": {"value": v, "unit": "GB/s", "cores": vals[0][1], "kind": "port",
-                                 "sample": vals[0][2]},
+                "data": "synthetic",
+                "config": {"workload": f"config1: {N_LAYERS} MoE decode layers (D=2688, F=1856, FS=3712, E=128, "
+                                       "top-6), B=1, z=0.90, one step = every layer with one of 8 rotating "
+                                       "input sets (the GPU arm's step)",
+                           "same_config": N_LAYERS == 23},
+                "cpu_baseline": {"value": v, "unit": "GB/s", "cores": cores, "kind": "port",
+                                 "sample": f"{n} full steps ({N_LAYERS} layers each, {N_SETS} rotating input sets) "
+                                           f"after {min(warmup, 3)} warm-up steps; C port of the reference "
+                                           f"decode kernel's algorithm (oracle/hsd_oracle.c), OpenMP {cores} "
+                                           f"threads; layouts built on the host by the oracle's transpose in "
+                                           f"{build_s:.0f} s (untimed)"},
                 "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-                "note": "the reference runs only on Apple silicon (MLX/Metal); this arm times the C port "
-                        "of its decode kernel's algorithm on the host cores"}
+                "note": "the reference runs only on Apple silicon (MLX/Metal); this arm times the C port of its "
+                        "decode kernel's algorithm on the host cores, and never loads libhsd.so"}
         print(json.dumps(line), flush=True)
         if dist_on:
             import torch.distributed as dist
@@ -558,8 +751,13 @@ def main():
 
     prefill = None
     if not args.no_prefill:
-        prefill = prefill_leg(layers, device, dist_on)
+        prefill = {"chunk512": prefill_leg(layers, device, dist_on),
+                   "chunk2048": prefill_leg(layers, device, dist_on, chunk=2048)}
     ep = ep_leg(layers, device, dist_on) if dist_on else None
+
+    mamba = None
+    if world == 1 and not args.no_mamba:
+        mamba = mamba_leg(device)
 
     model = None
     if world == 1 and not args.no_model:
@@ -567,10 +765,14 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        v, cores, sample = cpu_leg(layers, wl, budget_s=args.cpu_seconds)
-        cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+        host = host_layers_from_device(layers)
+        v, ms_cpu, cores, n = cpu_steps(host, host_inputs(wl.sets), 0, warmup=1, budget_s=args.cpu_seconds)
+        cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": f"{n} full steps ({N_LAYERS} layers, the workload's {N_SETS} rotating input sets), "
+                         f"{ms_cpu:.1f} ms per step, C port of the reference decode kernel's algorithm "
+                         f"(oracle/hsd_oracle.c), OpenMP {cores} threads"}
 
-    traffic = traffic_from_profile()
+    traffic, traffic_src = traffic_from_profile()
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": steps,
         "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
@@ -586,14 +788,15 @@ def main():
                           "y of step i down after it; the copy stream is joined before the end event"},
         "gpu_launches": steps * N_LAYERS,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                     "per_launch_bytes": per_launch_bytes, "launch_us": launch_ms * 1e3},
+                     "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
+                     "peak_kind": peak_kind, "per_launch_bytes": per_launch_bytes, "launch_us": launch_ms * 1e3},
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "us_per_layer": launch_ms * 1e3,
         "sweep": sweep,
         "prefill": prefill,
         "expert_parallel": ep,
+        "mamba": mamba,
         "model": model,
     }
     if rank == 0:
@@ -601,6 +804,9 @@ def main():
     if dist_on:
         import torch.distributed as dist
         dist.destroy_process_group()
+    if ep is not None and not ep["parity_ok"]:
+        print(f"expert-parallel parity FAILED: {ep}", file=sys.stderr, flush=True)
+        sys.exit(3)
 
 
 if __name__ == "__main__":

@@ -74,7 +74,7 @@ int hsd_swap_last2_u16(const uint16_t* in, uint16_t* out, int64_t lead, int64_t 
 
 /* ---- decode: hsd/decode.py ---------------------------------------------------- */
 
-/* hsd/decode.py:238 sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D,
+/* hsd/decode.py:164 sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D,
  * topk, sl, unr, nds, out_dtype, loadsc):
  *   h     [B, topk*F + FS] (h_dtype: bf16 / f16 / f32), the ReLU^2 activations of the
  *         selected experts then the shared expert's
@@ -311,7 +311,9 @@ int hsd_attn_decode(const void* q, int64_t q_stride, const void* kc, const void*
  * HSD_ERR_SHAPE with the bytes it needs (at the reference shapes: up to about 11 tokens;
  * a model with fewer experts or narrower layers admits more). The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture. Calls share the array: calls whose work
+ * make that first call before any stream capture. hsd_prefill_noalloc_max_bytes does the
+ * same look-up for the current device (when one is present), so calling it once per device
+ * does the set-up without inputs. Calls share the array: calls whose work
  * overlaps on the GPU (different streams or host threads) race; calls ordered on one
  * stream do not. Allocates nothing, frees nothing. */
 int hsd_prefill_noalloc_max_bytes(size_t* bytes);

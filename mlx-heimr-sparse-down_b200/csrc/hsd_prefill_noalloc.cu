@@ -97,10 +97,18 @@ int noalloc_layout(int T, int D, int F, int FS, int topk, int E, int NT, NoAlloc
 
 }  // namespace
 
+// Also looks up the array's address on the current device, so a caller can do the one-time
+// set-up without inputs (before a stream capture, for instance).
 extern "C" int hsd_prefill_noalloc_max_bytes(size_t* bytes) {
   if (!bytes) return hsd::set_error(HSD_ERR_ARG, "hsd_prefill_noalloc_max_bytes: null output");
   *bytes = kNoAllocScratchBytes;
-  return HSD_OK;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();                          // no device here: the size alone is the answer
+    return HSD_OK;
+  }
+  void* base = nullptr;
+  return scratch_address(&base);
 }
 
 extern "C" int hsd_sparse_down_prefill_noalloc(const void* h, int h_dtype, const float* gains,

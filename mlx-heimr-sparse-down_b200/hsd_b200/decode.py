@@ -13,7 +13,7 @@ from . import _lib
 
 def sparse_down(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS, D, topk,
                 sl=928, unr=2, nds=3, out_dtype=None, loadsc=1, resid=None, out=None, all_rows=False):
-    """hsd/decode.py:238 -- the down projection over the live rows only.
+    """hsd/decode.py:164 -- the down projection over the live rows only.
 
     h [B, topk*F + FS] (bf16 / f16 / f32), sel [B, topk] int32 (the routed experts),
     gains [B, topk+1] f32 (routing scores, then the shared expert's gain, 1) -> y [B, D].

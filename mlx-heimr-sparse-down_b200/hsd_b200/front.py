@@ -9,6 +9,9 @@ never synchronises with the host and can be captured in a CUDA graph.
 import torch
 
 from . import _lib
+from . import synth
+
+QGEMV_ROWS = 8          # rows up to which a 4-bit linear runs the matrix-vector kernel
 
 
 def moe_up(x, sel, uw, us, ub, suw, sus, sub, *, F, FS, D, topk, out_dtype=torch.bfloat16, out=None):
@@ -66,3 +69,49 @@ def qlinear(x, w, s, b, *, resid=None, out_dtype=None, out=None):
               _lib.ptr(b), _lib.dtype_code(s, what), _lib.ptr(resid), _lib.ptr(out), _lib.dtype_code(out, what),
               B, in_f, out_f, _lib.stream_of(x))
     return out
+
+
+def dequant_affine4(w, s, b, dtype=torch.bfloat16):
+    """Packed [.., R, C/8] words + [.., R, C/64] scales / biases -> [.., R, C] (fp32 s*q + b)."""
+    shifts = 4 * torch.arange(8, device=w.device, dtype=torch.int32)
+    q = (w.unsqueeze(-1) >> shifts) & 15
+    q = q.reshape(*w.shape[:-1], w.shape[-1] * 8).float()
+    R, C = q.shape[-2], q.shape[-1]
+    qg = q.view(*q.shape[:-1], C // 64, 64)
+    W = qg * s.float().unsqueeze(-1) + b.float().unsqueeze(-1)
+    return W.view(*q.shape[:-2], R, C).to(dtype)
+
+
+class QLinear:
+    """A 4-bit g64 linear (mlx QuantizedLinear): w [out, in/8], s / b [out, in/64]. Decode rows
+    (<= QGEMV_ROWS) use hsd_qlinear_decode on the packed weights; longer prompt chunks use a
+    dequantised bf16 copy with cuBLAS (kept when bf16_copy)."""
+
+    def __init__(self, out_f, in_f, gen, device, std, bf16_copy=True):
+        """Seeded random weights N(0, std), quantised."""
+        w, s, b = synth.quantized_weights((out_f, in_f), gen, device, std=std)
+        self._set(w, s, b, bf16_copy)
+
+    @classmethod
+    def from_packed(cls, w, s, b, bf16_copy=True):
+        """Existing packed weights w [out, in/8] u32, s / b [out, in/64]."""
+        q = cls.__new__(cls)
+        q._set(w, s, b, bf16_copy)
+        return q
+
+    def _set(self, w, s, b, bf16_copy):
+        self.w, self.s, self.b = w, s, b
+        self.out_f, self.in_f = w.shape[0], w.shape[1] * 8
+        self.dq = dequant_affine4(w, s, b) if bf16_copy else None
+
+    def dequant_f32(self):
+        """The dequantised weights in fp32 (s*q + b), [out, in]."""
+        return dequant_affine4(self.w, self.s, self.b, torch.float32)
+
+    def __call__(self, x, resid=None, out_dtype=None):
+        if x.shape[0] <= QGEMV_ROWS or self.dq is None:
+            return qlinear(x, self.w, self.s, self.b, resid=resid, out_dtype=out_dtype)
+        y = x @ self.dq.t()
+        if resid is not None:
+            y = (resid.float() + y.float()).to(resid.dtype)
+        return y if out_dtype is None else y.to(out_dtype)

@@ -10,31 +10,38 @@ state after row n of a verify equals n single steps bit for bit.
 
 The cache is a two-entry list like mlx-lm's ArraysCache: cache[0] the conv window
 [K-1, conv_dim] (bf16, None at the start), cache[1] the SSM state [H, P, N] (fp32, None
-at the start). in_proj / out_proj / the norms are dense torch ops on the block's weights;
-the causal conv, the selective scan and the rollback are this library's kernels.
+at the start). Every piece of the block runs this library's kernels: in_proj / out_proj are
+4-bit g64 linears like the reference checkpoint's QuantizedLinear (hsd_qlinear_decode for
+verify and decode rows, the residual added inside out_proj's kernel; prompt chunks longer
+than 8 rows use the linear's dequantised bf16 copy), the pre-norm and the gated norm are
+hsd_rms_norm / hsd_gated_rms_norm, and the causal conv, the selective scan and the rollback
+are csrc/hsd_mamba.cu.
 """
 from dataclasses import dataclass
 
 import torch
 
 from . import _lib
+from .front import QLinear
+from .rowops import gated_rms_norm, rms_norm
 
 
 @dataclass
 class Mamba2Block:
     """One Mamba-2 block (pre-norm + mixer) of the Nemotron-H layer stack.
 
-    norm_w [D]; in_proj [I + conv_dim + H, D] (gate | conv input | dt); conv_w [conv_dim, K]
-    f32, conv_b [conv_dim] f32; A_log, D, dt_bias [H] f32; gate_norm_w [I]; out_proj [D, I]."""
+    norm_w [D]; in_proj a 4-bit linear [I + conv_dim + H, D] (gate | conv input | dt); conv_w
+    [conv_dim, K] f32, conv_b [conv_dim] f32; A_log, D, dt_bias [H] f32; gate_norm_w [I];
+    out_proj a 4-bit linear [D, I]."""
     norm_w: torch.Tensor
-    in_proj: torch.Tensor
+    in_proj: QLinear
     conv_w: torch.Tensor
     conv_b: torch.Tensor
     A_log: torch.Tensor
     D: torch.Tensor
     dt_bias: torch.Tensor
     gate_norm_w: torch.Tensor
-    out_proj: torch.Tensor
+    out_proj: QLinear
     H: int
     P: int
     G: int
@@ -54,41 +61,23 @@ class Mamba2Block:
 
 def random_mamba2(seed, hidden=2688, H=64, P=64, G=8, N=128, K=4, device="cuda", dtype=torch.bfloat16,
                   std=0.02):
-    """A seeded random-init block with the reference model's Mamba-2 shapes."""
+    """A seeded random-init block with the reference model's Mamba-2 shapes; the linears'
+    weights N(0, std) quantised to 4-bit g64."""
     gen = torch.Generator(device=device).manual_seed(seed)
     I = H * P
     conv_dim = I + 2 * G * N
 
-    def rnd(*shape, s=std):
-        return (torch.randn(shape, generator=gen, device=device) * s).to(dtype)
-
     return Mamba2Block(
         norm_w=(1.0 + 0.1 * torch.randn(hidden, generator=gen, device=device)).to(dtype),
-        in_proj=rnd(I + conv_dim + H, hidden),
+        in_proj=QLinear(I + conv_dim + H, hidden, gen, device, std),
         conv_w=torch.randn((conv_dim, K), generator=gen, device=device) * 0.3,
         conv_b=torch.randn(conv_dim, generator=gen, device=device) * 0.1,
         A_log=torch.log(torch.linspace(1.0, 16.0, H, device=device)),
         D=torch.ones(H, device=device),
         dt_bias=torch.linspace(-4.0, -1.0, H, device=device),
         gate_norm_w=(1.0 + 0.1 * torch.randn(I, generator=gen, device=device)).to(dtype),
-        out_proj=rnd(hidden, I),
+        out_proj=QLinear(hidden, I, gen, device, std),
         H=H, P=P, G=G, N=N, K=K)
-
-
-def rms_norm(x, w, eps):
-    """weight * (x / rms(x)) in fp32, cast back to x's dtype before the weight (NemotronH's)."""
-    xf = x.float()
-    xf = xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)
-    return w * xf.to(x.dtype)
-
-
-def gated_rms_norm(y, gate, w, group_size, eps, out_dtype):
-    """y * silu(gate), RMS-normalised per group of group_size, times the weight."""
-    yf = y.float() * torch.nn.functional.silu(gate.float())
-    *lead, last = yf.shape
-    g = yf.view(*lead, last // group_size, group_size)
-    g = g * torch.rsqrt(g.square().mean(-1, keepdim=True) + eps)
-    return w * g.view(*lead, last).to(out_dtype)
 
 
 def conv_verify(conv_in, conv_state, conv_w, conv_b, out_dtype=torch.bfloat16):
@@ -137,7 +126,7 @@ def mamba_verify(block, x3, cache, records, checkpoints=True):
     L = x.shape[0]
     I, Cd = b.I, b.conv_dim
     h = rms_norm(x, b.norm_w, b.eps)
-    proj = h @ b.in_proj.t()                                      # [L, I + conv_dim + H]
+    proj = b.in_proj(h)                                           # [L, I + conv_dim + H]
     co, padded = conv_verify(proj[:, I:I + Cd], cache[0], b.conv_w, b.conv_b)
     y, states = ssm_verify(co, proj[:, I + Cd:], b.A_log, b.D, b.dt_bias, cache[1], H=b.H, P=b.P, G=b.G, N=b.N,
                            time_step_limit=b.time_step_limit, checkpoints=checkpoints)
@@ -146,7 +135,7 @@ def mamba_verify(block, x3, cache, records, checkpoints=True):
     if checkpoints:
         records.append((cache, padded, states, b.K))
     yn = gated_rms_norm(y, proj[:, :I], b.gate_norm_w, I // b.G, b.eps, x.dtype)
-    return x3 + (yn @ b.out_proj.t())[None]
+    return b.out_proj(yn, resid=x)[None]                          # x3 + out_proj(yn), one rounding
 
 
 def mamba_rollback(records, n_keep):
@@ -226,12 +215,12 @@ def mamba_step_resident(block, x, rc, n_keep):
     b = block
     I, Cd = b.I, b.conv_dim
     h = rms_norm(x, b.norm_w, b.eps)
-    proj = h @ b.in_proj.t()
+    proj = b.in_proj(h)
     co = conv_step(proj[:, I:I + Cd], rc.padded, n_keep, b.conv_w, b.conv_b)
     y = ssm_step(co, proj[:, I + Cd:], b.A_log, b.D, b.dt_bias, rc.states, n_keep, H=b.H, P=b.P, G=b.G, N=b.N,
                  time_step_limit=b.time_step_limit)
     yn = gated_rms_norm(y, proj[:, :I], b.gate_norm_w, I // b.G, b.eps, x.dtype)
-    return x + yn @ b.out_proj.t()
+    return b.out_proj(yn, resid=x)
 
 
 def rollback_into(padded, states, n_keep, conv_out, state_out):

@@ -36,13 +36,12 @@ import torch
 from . import mamba as hm
 from . import synth
 from .decode import dense_down, sparse_down
-from .front import moe_up, qlinear
+from .front import QGEMV_ROWS, QLinear, moe_up
 from .layout import to_neuron_major
 from .prefill import sparse_down_prefill
 from .rowops import DecodeAttention, Router, gated_rms_norm, rms_norm
 
 MODES = ("dense", "sparse", "stock")
-QGEMV_ROWS = 8          # rows up to which the linears use the 4-bit matrix-vector kernel
 
 
 def layer_pattern(n_layers=52, n_moe=23, n_attn=6):
@@ -103,36 +102,6 @@ class ModelArgs:
         return cls(hidden=384, vocab=2048, n_layers=8, n_moe=3, n_attn=2, E=16, topk=4, F=256, FS=512,
                    mamba_heads=8, mamba_head_dim=32, mamba_groups=2, mamba_state=64, q_heads=4, kv_heads=2,
                    head_dim=64, max_len=1024, pattern="ME*MEM*E")
-
-
-def dequant_affine4(w, s, b, dtype=torch.bfloat16):
-    """Packed [.., R, C/8] words + [.., R, C/64] scales / biases -> [.., R, C] (fp32 s*q + b)."""
-    shifts = 4 * torch.arange(8, device=w.device, dtype=torch.int32)
-    q = (w.unsqueeze(-1) >> shifts) & 15
-    q = q.reshape(*w.shape[:-1], w.shape[-1] * 8).float()
-    R, C = q.shape[-2], q.shape[-1]
-    qg = q.view(*q.shape[:-1], C // 64, 64)
-    W = qg * s.float().unsqueeze(-1) + b.float().unsqueeze(-1)
-    return W.view(*q.shape[:-2], R, C).to(dtype)
-
-
-class QLinear:
-    """A 4-bit g64 linear (mlx QuantizedLinear): w [out, in/8], s / b [out, in/64]. Decode rows
-    (<= QGEMV_ROWS) use hsd_qlinear_decode on the packed weights; longer prompt chunks use a
-    dequantised bf16 copy with cuBLAS (kept when bf16_copy)."""
-
-    def __init__(self, out_f, in_f, gen, device, std, bf16_copy=True):
-        self.out_f, self.in_f = out_f, in_f
-        self.w, self.s, self.b = synth.quantized_weights((out_f, in_f), gen, device, std=std)
-        self.dq = dequant_affine4(self.w, self.s, self.b) if bf16_copy else None
-
-    def __call__(self, x, resid=None, out_dtype=None):
-        if x.shape[0] <= QGEMV_ROWS or self.dq is None:
-            return qlinear(x, self.w, self.s, self.b, resid=resid, out_dtype=out_dtype)
-        y = x @ self.dq.t()
-        if resid is not None:
-            y = (resid.float() + y.float()).to(resid.dtype)
-        return y if out_dtype is None else y.to(out_dtype)
 
 
 class MoEBlock:
@@ -258,14 +227,14 @@ class MambaLayer:
         self.out_proj = QLinear(a.hidden, I, gen, device, a.std)
         self.blk = hm.Mamba2Block(
             norm_w=(1.0 + 0.1 * torch.randn(a.hidden, generator=gen, device=device)).to(torch.bfloat16),
-            in_proj=self.in_proj.dq,
+            in_proj=self.in_proj,
             conv_w=torch.randn((conv_dim, K), generator=gen, device=device) * 0.3,
             conv_b=torch.randn(conv_dim, generator=gen, device=device) * 0.1,
             A_log=torch.log(torch.linspace(1.0, 16.0, H, device=device)),
             D=torch.ones(H, device=device),
             dt_bias=torch.linspace(-4.0, -1.0, H, device=device),
             gate_norm_w=(1.0 + 0.1 * torch.randn(I, generator=gen, device=device)).to(torch.bfloat16),
-            out_proj=self.out_proj.dq,
+            out_proj=self.out_proj,
             H=H, P=P, G=G, N=N, K=K, eps=a.eps)
 
     def _mix(self, x, conv_scan):

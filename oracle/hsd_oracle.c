@@ -26,18 +26,21 @@ static inline float bf16f(uint16_t b) {
   return v.f;
 }
 
+/* One nibble at a time; the threads split the output rows (l, c), each of which only its
+ * own thread writes. */
 void oracle_nibble_transpose(const uint32_t* w, uint32_t* out, int64_t lead, int64_t R, int64_t CW) {
   const int64_t C = CW * 8, OW = R / 8;
-  for (int64_t l = 0; l < lead; ++l) {
-    const uint32_t* src = w + l * R * CW;
-    uint32_t* dst = out + l * C * OW;
-    memset(dst, 0, sizeof(uint32_t) * (size_t)(C * OW));
-    for (int64_t r = 0; r < R; ++r)
-      for (int64_t c = 0; c < C; ++c) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t l = 0; l < lead; ++l)
+    for (int64_t c = 0; c < C; ++c) {
+      const uint32_t* src = w + l * R * CW;
+      uint32_t* dst = out + (l * C + c) * OW;
+      memset(dst, 0, sizeof(uint32_t) * (size_t)OW);
+      for (int64_t r = 0; r < R; ++r) {
         const uint32_t q = (src[r * CW + c / 8] >> (4 * (c % 8))) & 0xFu;
-        dst[c * OW + r / 8] |= q << (4 * (r % 8));
+        dst[r / 8] |= q << (4 * (r % 8));
       }
-  }
+    }
 }
 
 /* One (token, slot, slice) x output words [w_lo, w_hi): adds gain * slice result to yrow. */

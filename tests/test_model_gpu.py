@@ -11,10 +11,11 @@ from conftest import f32_np, rel_err
 from hsd_b200.model import ModelArgs, MTPHead, NemotronModel, identical_prefix
 
 B, N = 4, 2            # verify rows, rollback target (tests/test_verify_rollback.py:308-309)
-BOUND = 5e-2           # the reference's bf16-level bounds for residuals and caches
+BOUND = 5e-2           # the reference's bf16-level bound, kept for the residual stream
+STATE_BOUND = 1e-3     # rolled-back Mamba / conv / KV states against single steps (the north star's bar)
 
 
-def compare_states(model, sa, sb):
+def compare_states(model, sa, sb, bound=STATE_BOUND):
     assert int(sa.pos.item()) == int(sb.pos.item())
     o = int(sa.pos.item())
     diff = {"mamba_state": 0.0, "conv": 0.0, "kv": 0.0}
@@ -30,7 +31,7 @@ def compare_states(model, sa, sb):
                 mag["kv"] = max(mag["kv"], float(y.float().abs().max()))
     worst = {k: diff[k] / mag[k] for k in diff}
     for k, v in worst.items():
-        assert v < BOUND, (k, v)
+        assert v <= bound, (k, v)
     return worst
 
 
@@ -88,6 +89,29 @@ def test_rollback_then_single_steps(setup):
 
 
 @pytest.mark.gpu
+def test_verify_and_rollback_are_bit_identical_to_single_steps(setup):
+    """What the design claims, asserted exactly: every decode-row kernel computes a row
+    independently of the launch's other rows, and the Mamba checkpoints are the states the
+    single steps produce, so the verify rows, the rolled-back states and the steps taken after
+    a rollback equal single steps bit for bit (bound 0, not 1e-3)."""
+    model, st0, xin = setup
+    xb, sb = single_steps(model, st0, xin, B)
+    sa = st0.clone()
+    xa = model.verify_step(xin, sa)
+    assert torch.equal(xa, xb)
+    model.rollback(sa, B, B)
+    compare_states(model, sa, sb, bound=0.0)
+    _, sd = single_steps(model, st0, xin, N)
+    se = st0.clone()
+    model.verify_step(xin, se)
+    model.rollback(se, N, B)
+    compare_states(model, se, sd, bound=0.0)
+    for i in range(N, B):
+        model.step(xin[i:i + 1], se)
+    compare_states(model, se, sb, bound=0.0)
+
+
+@pytest.mark.gpu
 def test_graph_replay_equals_eager(cuda):
     """The captured step and the captured MTP iteration replay exactly the eager ops."""
     model = NemotronModel(ModelArgs.tiny(), seed=5, device=cuda, mode="sparse")
@@ -131,14 +155,25 @@ def test_dense_sparse_mtp_greedy_tokens_identical(cuda):
 
 
 @pytest.mark.gpu
-def test_stock_and_gemm_prefill_agree_to_a_near_tie(cuda):
-    """The checkpoint-layout dense kernel and the tensor-core prefill compute in other
-    orders, so their tokens agree until an argmax near-tie (the reference's bound: 10)."""
-    model = NemotronModel(ModelArgs.tiny(), seed=11, device=cuda, mode="stock")
-    gen = torch.Generator(device=cuda).manual_seed(12)
+@pytest.mark.parametrize("seed", [11, 21, 31])
+def test_stock_dense_path_agrees_with_sparse_for_10_tokens(cuda, seed):
+    """The stock dense path (hsd_dense_down_decode on the checkpoint layout, a different
+    kernel with another summation order) and the sparse path give the same greedy tokens for
+    at least 10 tokens -- the reference's bar over 24 tokens (tests/test_end_to_end.py:22-23,66-77) -- with the
+    prompt on the decode kernels in both modes; then also with the sparse prompt on the tensor-core
+    prefill GEMM. The smallest top-1 minus top-2 logit margin of the compared tokens is
+    reported beside the result."""
+    model = NemotronModel(ModelArgs.tiny(), seed=seed, device=cuda, mode="stock")
+    model.prefill_gemm = False
+    gen = torch.Generator(device=cuda).manual_seed(seed + 1)
     prompt = torch.randint(0, model.args.vocab, (16,), generator=gen, device=cuda).tolist()
     stock, st = model.generate(prompt, 24)
     model.set_mode("sparse")
     sparse, _ = model.generate(prompt, 24)
-    n = identical_prefix(stock, sparse)
-    assert n >= 10 or min(st["margins"][:n + 1]) < 0.05, (n, stock, sparse)
+    model.prefill_gemm = True
+    gemm, _ = model.generate(prompt, 24)
+    n, ng = identical_prefix(stock, sparse), identical_prefix(stock, gemm)
+    print(f"seed {seed}: stock = sparse for {n} tokens, = sparse with GEMM prefill for {ng}; "
+          f"min top-2 margin over them {min(st['margins'][:max(n, ng)]):.3e}")
+    assert n >= 10, (n, stock, sparse)
+    assert ng >= 10, (ng, stock, gemm)

@@ -18,6 +18,27 @@ from hsd_b200 import prefill as hp
 from hsd_b200 import synth
 
 TOL = 5e-3        # the prefill tolerance of tests/test_prefill_gpu.py
+REF = dict(D=2688, F=1856, FS=3712, topk=6, E=128)   # the reference model's MoE shapes
+
+
+def scratch_bytes(T, D, F, FS, topk, E, tt=hp.GEMM_TT):
+    """The scratch a call needs, as the library lays it out: the compacted tile order (at most
+    every full tile of slots + one partial tile per expert with slots + the shared expert's
+    tiles), the fp16 A rows of those tiles and the fp32 partial rows."""
+    nr, ns = hp.num_tiles(T, topk, E, tt)
+    slots = T * topk
+    nc = min(nr, slots // tt + min(E, slots)) + ns
+    up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    hc_off = up(up(4 * nc) + 4 * nc * tt)
+    part_off = up(hc_off + nc * tt * max(F, FS) * 2)
+    return part_off + T * (topk + 1) * D * 4
+
+
+def largest_chunk(cap, **shape):
+    T = 1
+    while scratch_bytes(T + 1, **shape) <= cap:
+        T += 1
+    return T
 
 
 def _args(c, lay, tiles, y):
@@ -58,6 +79,29 @@ def test_noalloc_matches_workspace_entry_two_calls(cuda):
         torch.cuda.synchronize()
         assert rel_err(f32_np(y), f32_np(y_ref)) < TOL
         assert hsd_b200.device_status() == 0
+
+
+@pytest.mark.gpu
+def test_noalloc_largest_chunk_that_fits(cuda):
+    """The largest chunk the fixed scratch admits at the reference shapes (its A rows reach the
+    end of the array) equals the workspace entry point; one token more is refused."""
+    cap = ctypes.c_size_t(0)
+    L.call("hsd_prefill_noalloc_max_bytes", ctypes.byref(cap))
+    T = largest_chunk(cap.value, **REF)
+    assert scratch_bytes(T, **REF) > cap.value - (1 << 20)      # the end of the array is in use
+    c = synth.decode_case(seed=53, B=T, zero_frac=0.9, routing="zipf", device=cuda)
+    lay = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"]) + hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
+    tiles = hp.build_tiles(c["sel"], c["E"], hp.GEMM_TT)
+    y_ref = _existing(c, lay, tiles)
+    y = _noalloc(c, lay, tiles)
+    torch.cuda.synchronize()
+    assert rel_err(f32_np(y), f32_np(y_ref)) < TOL
+    assert hsd_b200.device_status() == 0
+    c2 = synth.decode_case(seed=54, B=T + 1, zero_frac=0.9, routing="zipf", device=cuda)
+    tiles2 = hp.build_tiles(c2["sel"], c2["E"], hp.GEMM_TT)
+    y2 = torch.empty((T + 1, c2["D"]), dtype=torch.float32, device=cuda)
+    rc = L.lib().hsd_sparse_down_prefill_noalloc(*_args(c2, lay, tiles2, y2), L.stream_of(c2["h"]))
+    assert rc == L.HSD_ERR_SHAPE
 
 
 def test_noalloc_refuses_a_chunk_that_does_not_fit():
