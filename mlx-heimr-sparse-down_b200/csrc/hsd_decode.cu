@@ -8,50 +8,41 @@
 //   The token's 64-neuron groups are listed slot by slot (topk routed experts, then the
 //   shared expert): GT = topk*F/64 + FS/64 groups (232 at the reference shapes); they are
 //   the contiguous 64-column blocks of h's row. The D outputs are cut into chunks of C
-//   outputs (C/2 contiguous bytes of every neuron row). A thread-block CLUSTER of 8 CTAs
-//   owns one (token, chunk); CTA `rank` owns groups [rank*GT/8, (rank+1)*GT/8) -- at the
-//   reference shapes one routed expert or one half of the shared expert (29 groups). The 8
-//   partial outputs are summed through distributed shared memory in a fixed rank order:
-//   deterministic, with no scratch memory, atomics or second kernel.
+//   outputs (C/2 contiguous bytes of every neuron row, one 4-byte word per lane). A
+//   thread-block CLUSTER of 8 CTAs owns one (token, chunk); CTA `rank` owns groups
+//   [rank*GT/8, (rank+1)*GT/8) -- at the reference shapes one routed expert or one half of
+//   the shared expert (29 groups). The 8 partial outputs are summed through distributed
+//   shared memory in a fixed rank order: deterministic, with no scratch memory, atomics or
+//   second kernel.
 //
-// Per CTA and batch of up to 32 groups:
-//   1. one 16-byte load per thread brings the batch's h columns (and each group's expert
-//      id and gain) into shared memory;
-//   2. each warp builds its groups' live masks with two ballots and, for a live group,
-//      starts the copies of the group's scale and bias chunks (C*2 bytes each) as 16-byte
-//      cp.async pieces, one per lane;
-//   3. every warp scans the live counts, cuts the live rows into sub-batches of whole groups
-//      of at most SBR rows, and compacts its groups' live rows into an ascending list
-//      (ballot prefix popcounts); each lane holding a live row of one of the first `slots`
-//      sub-batches starts the copy of that row's C/2-byte chunk into the sub-batch's slot of
-//      the shared-memory ring as one TMA bulk copy. The TMA unit takes one bulk copy about
-//      every 16 cycles, which makes the issue of the ~200 row copies per CTA the longest
-//      phase of a token's chain; the scale/bias pieces of step 2 go over the load/store
-//      path, beside it, instead of adding ~60 bulk copies to that queue. A slot's copies
-//      complete on the slot's mbarrier: one arrival carries the sub-batch's TMA bytes, and
-//      every thread adds one arrival that fires when its own cp.async pieces have landed;
-//   4. per sub-batch, as its slot's mbarrier completes: thread (word wp, group lane gl)
-//      walks the live rows of its groups gl, gl+NGL, ... of the sub-batch in shared memory,
-//      accumulating acc'[n] = sum h * (1 + q_n/16) and hsum = sum h in fp32, and folds each
-//      group in as out[n] += g * (16*s[n]*(acc'[n] - hsum) + b[n]*hsum) -- the reference's
-//      affine algebra (s * sum(h q) + b * sum(h)); 1 + q/16 is built exactly from the
-//      nibble with bit operations, sparing an integer-to-float conversion per weight. The
-//      computation of a sub-batch overlaps the landing of the later ones; a slot freed is
-//      refilled with the sub-batch `slots` places later;
-//   5. the NGL group lanes are reduced in shared memory in a fixed order;
-//   6. each CTA pushes the 8 slices of its partial chunk to their owner CTAs with st.async
-//      (completing on the owner's mbarrier), and each owner sums its slice's 8 partials in
-//      rank order: one cluster handshake (at the start) instead of two cluster barriers.
-// A lane's groups are folded in ascending order whatever the sub-batch cut, and a group's
-// rows always form one sub-batch, so the result depends neither on the ring's size nor on
-// the other groups' live counts: the dense form (every row live) and the sparse form give
-// the same bits, and so do every stage size chosen per batch size below.
-// Weights are streamed with an L2 evict-first policy (they are not reused by the step).
-// The launch uses programmatic dependent launch: the kernel releases its dependents at
-// once and waits (griddepcontrol.wait) for the previous kernel before its first read, so
-// back-to-back layers overlap launch latency with the previous layer's tail. Every
-// mbarrier wait is bounded (2 s of %globaltimer); running out sets HSD_ERR_TIMEOUT in the
-// status word, waits once more (bounded) for the copies in flight and finishes.
+// Per CTA: 16 group lanes, lane L folding the CTA's groups L, L+16, L+32, ... in ascending
+// order into its own 8 outputs per word; a warp runs one or two group lanes (16 or 8 warps),
+// lane w of the warp owning word w of the chunk. Per round a warp takes two groups per group
+// lane and, with no shared-memory staging:
+//   1. loads the groups' h values (two per lane, one coalesced load per group), expert ids
+//      and gains, and builds each group's live mask with two ballots;
+//   2. starts, for every live group, the 16-byte cp.async copies of its scale and bias
+//      chunks into the warp's own shared-memory area, and loads the first RG live rows of
+//      every group straight into registers -- one coalesced 4-byte load per lane and row, all
+//      of them issued before any is used, so a round costs one memory round trip whatever
+//      the number of rows (a group with more than RG live rows takes further round trips);
+//   3. accumulates acc'[n] = sum h * (1 + q_n/16) and hsum = sum h over each group's live
+//      rows in ascending order (1 + q/16 built exactly from the nibble with bit operations,
+//      packed fp32 FMAs), and folds the group in as out[n] += g * (16*s[n]*(acc'[n] - hsum)
+//      + b[n]*hsum) -- the reference's affine algebra s * sum(h q) + b * sum(h).
+// Then the 16 group lanes are reduced in shared memory in a fixed order, and each CTA pushes
+// the 8 slices of its partial chunk to their owner CTAs with st.async (completing on the
+// owner's mbarrier); each owner sums its slice's 8 partials in rank order.
+// A token's arithmetic depends only on C: the group lanes, their fold order and both
+// reduction trees are fixed, whatever the batch size, the warp count or the live counts,
+// and a row dead in the token is never touched. So a row of any batch equals the same token
+// decoded alone bit for bit, and the dense form (every row live) adds an exact zero where
+// the sparse form skips a row: both give the same bits.
+// Weights are read with an L2 evict-first policy (they are not reused by the step). The
+// launch uses programmatic dependent launch: the kernel releases its dependents at once and
+// waits (griddepcontrol.wait) for the previous kernel before its first read, so back-to-back
+// layers overlap launch latency with the previous layer's tail. The one mbarrier wait is
+// bounded (2 s of %globaltimer); running out sets HSD_ERR_TIMEOUT in the status word.
 #include <cooperative_groups.h>
 #include <cstdlib>
 
@@ -64,20 +55,8 @@ HSD_DEFINE_STATUS(decode)
 namespace {
 
 constexpr int kCluster = 8;    // CTAs per (token, chunk)
-constexpr int kGB = 32;        // groups per batch
 constexpr int kGS = 64;        // quantisation group size
-constexpr int kMaxSlots = 8;   // sub-batch slots (mbarriers) of the staging ring
-
-template <int C>
-struct DecodeCfg {
-  static constexpr int NWC = C / 8;                    // words of one row in a chunk
-  static constexpr int THREADS = 512;                  // 16 full warps (ballots use full masks)
-  static constexpr int WARPS = THREADS / 32;
-  static constexpr int NGL = WARPS;                    // group lanes: one warp each, a lane per word
-  static_assert(NWC <= 32, "a chunk row must fit one warp");
-  static constexpr int MAX_RB = 1024;                  // largest staging ring, in rows
-  static constexpr int MIN_RB = NGL * 8;               // the group-lane partials reuse the ring
-};
+constexpr int kNGL = 16;       // group lanes per CTA (fixed: it sets the arithmetic)
 
 struct DecodeParams {
   const void* h;
@@ -96,74 +75,118 @@ struct DecodeParams {
   int NR;    // columns of h: topk*F + FS
   int GT;    // groups per token
   int NW;    // words per neuron row: D/8
-  int SBR;   // rows per ring slot = the sub-batch limit (>= 64: a group's rows fit one slot)
-  int nring; // slots of the staging ring (ring rows = SBR * nring), 1..kMaxSlots
 };
 
-// The staging ring (SBR*nring rows of NWC words, also the group-lane partials) follows this
-// struct in dynamic shared memory, at a 128-byte boundary.
-template <int C>
+// Shared memory of one CTA (dynamic, possibly padded by the host to limit CTAs per SM).
+template <int C, int RG>
 struct DecodeSmem {
-  using Cfg = DecodeCfg<C>;
-  uint16_t meta_s[kGB * C];                     // staged scale chunks (16-bit)
-  uint16_t meta_b[kGB * C];                     // staged bias chunks
-  float hs[kGB * kGS];                          // the batch's h values (fp32)
-  float hrow[kGB * kGS];                        // h of each compacted live row
-  uint16_t rows[kGB * kGS];                     // compacted live rows: (group in batch) << 6 | neuron
-  unsigned long long gmask[kGB];
-  unsigned long long bars[kMaxSlots];           // completion of each slot's bulk copies
-  unsigned long long rbar;                      // arrival of the 8 partial slices (st.async)
-  int gcnt[kGB], goff[kGB + 1];
-  int sbeg[kGB + 1];                            // sub-batch starts (rows); sbeg[nsb] = nrows
-  int gsrc[kGB];                                // expert id, -1 = shared expert, -2 = invalid
-  int gloc[kGB];                                // the group's index inside its expert
-  float ggain[kGB];
+  uint32_t stage[kNGL][2][RG][C / 8];           // per warp and group of a round: staged live rows
+  uint16_t meta[kNGL][2][2][C];                 // per warp and group of a round: scale, bias chunks
+  uint32_t ch[kNGL][2][64];                     // per warp and group: h (raw bits) of the compacted live rows
+  short cj[kNGL][2][64];                        //   ... and their rows
+  float red[kNGL][C];                           // the group lanes' partial chunks
   float part[C];                                // this CTA's partial output chunk
   float recv[C];                                // [rank][C/8]: the slices pushed to this CTA
+  uint32_t hs[2 * kNGL][64];                    // the round's h values (raw; 64 entries of up to 4 bytes)
+  int gsrc[2 * kNGL];                           // the round's expert ids (-1 shared, -2 none)
+  float ggain[2 * kNGL];                        // and gains
+  unsigned long long rbar;                      // arrival of the 8 partial slices (st.async)
+  unsigned long long mbar[kNGL];                // per warp: its round's scale / bias copies
 };
 
-template <int C>
-constexpr size_t ring_offset() {
-  return (sizeof(DecodeSmem<C>) + 127) / 128 * 128;
-}
-
-// Live mask of 64 h values (two per lane) with two ballots.
-__device__ __forceinline__ unsigned long long ballot64(bool nz0, bool nz1) {
-  const unsigned lo = __ballot_sync(0xffffffffu, nz0);
-  const unsigned hi = __ballot_sync(0xffffffffu, nz1);
-  return (static_cast<unsigned long long>(hi) << 32) | lo;
-}
-
-// Index of this lane's entry (j = lane or lane + 32) among the live entries of mask.
-__device__ __forceinline__ int live_prefix(unsigned long long mask, int j) {
-  const unsigned long long below = (j == 0) ? 0ull : (mask & ((1ull << j) - 1ull));
-  return __popcll(below);
-}
-
-// 1 + q/16 for the nibble of q at bit offset 4n, exact: q lands in mantissa bits 19..22.
-template <int N>
-__device__ __forceinline__ float nib_unit(uint32_t q) {
-  constexpr int sh = 19 - 4 * N;
-  const uint32_t m = (sh >= 0) ? (q << (sh >= 0 ? sh : 0)) : (q >> (sh < 0 ? -sh : 0));
-  return __uint_as_float((m & 0x00780000u) | 0x3F800000u);
-}
-
-// (x, y) = (fma(h, u, x), fma(h, v, y)), each rounded to nearest as fmaf does: one packed
-// fp32 FMA (fma.rn.f32x2, sm_100) in place of two, the same bits
-__device__ __forceinline__ void ffma2(float& x, float& y, float h, float u, float v) {
-  asm("{\n .reg .b64 a, b, c;\n mov.b64 a, {%2, %2};\n mov.b64 b, {%3, %4};\n mov.b64 c, {%0, %1};\n"
-      " fma.rn.f32x2 c, a, b, c;\n mov.b64 {%0, %1}, c;\n}"
-      : "+f"(x), "+f"(y) : "f"(h), "f"(u), "f"(v));
-}
-
+// ---- the row arithmetic. A weight word packs the nibbles q_0..q_7 of 8 consecutive outputs
+// (low nibble first). Each nibble becomes the exact value 8 + q/2 in h's precision by one shift
+// and one mask-and-or -- two at a time for 16-bit h (bf16 0x4100 | q << 3, f16 0x4800 | q << 6),
+// one at a time for fp32 h (0x41000000 | q << 19) -- and the row adds h * (8 + q_n/2) to acc[n]
+// and h to hsum with fp32 FMAs (for 16-bit h mixed-precision ones): every product is exact and
+// every sum is rounded to nearest in fp32, so acc is exactly 8x the sum of h * (1 + q/16) that
+// a plain fp32 formulation would form, rounding for rounding. A group then contributes
+// 2*s * (acc - 8*hsum) + b*hsum: the reference's s * sum(h q) + b * sum(h), with acc - 8*hsum
+// exact (the two are within a factor 2 of each other).
 template <typename HT>
-__device__ __forceinline__ float load_h(const void* h, int64_t idx) {
-  return hsd::to_f32<HT>(reinterpret_cast<const HT*>(h)[idx]);
-}
+struct RowMath;
 
-// ---- mbarrier / bulk-copy helpers
+template <>
+struct RowMath<__nv_bfloat16> {
+  // raw: the row's h as bf16 bits in the low half
+  static __device__ __forceinline__ void row(float (&acc)[8], float& hsum, uint32_t raw, uint32_t w) {
+    const uint32_t v0 = ((w << 3) & 0x00780078u) | 0x41004100u;   // outputs 0, 4
+    const uint32_t v1 = ((w >> 1) & 0x00780078u) | 0x41004100u;   // 1, 5
+    const uint32_t v2 = ((w >> 5) & 0x00780078u) | 0x41004100u;   // 2, 6
+    const uint32_t v3 = ((w >> 9) & 0x00780078u) | 0x41004100u;   // 3, 7
+    asm("{\n .reg .b16 a0, a1, a2, a3, a4, a5, a6, a7, hh, one;\n"
+        " mov.b32 {a0, a4}, %10;\n mov.b32 {a1, a5}, %11;\n mov.b32 {a2, a6}, %12;\n mov.b32 {a3, a7}, %13;\n"
+        " mov.b32 {hh, _}, %9;\n mov.b16 one, 0x3F80;\n"
+        " fma.rn.f32.bf16 %0, hh, a0, %0;\n fma.rn.f32.bf16 %1, hh, a1, %1;\n"
+        " fma.rn.f32.bf16 %2, hh, a2, %2;\n fma.rn.f32.bf16 %3, hh, a3, %3;\n"
+        " fma.rn.f32.bf16 %4, hh, a4, %4;\n fma.rn.f32.bf16 %5, hh, a5, %5;\n"
+        " fma.rn.f32.bf16 %6, hh, a6, %6;\n fma.rn.f32.bf16 %7, hh, a7, %7;\n"
+        " fma.rn.f32.bf16 %8, hh, one, %8;\n}"
+        : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3]), "+f"(acc[4]), "+f"(acc[5]), "+f"(acc[6]),
+          "+f"(acc[7]), "+f"(hsum)
+        : "r"(raw), "r"(v0), "r"(v1), "r"(v2), "r"(v3));
+  }
+  static __device__ __forceinline__ bool live(uint32_t raw) { return (raw & 0x7FFFu) != 0u; }
+};
+
+template <>
+struct RowMath<__half> {
+  static __device__ __forceinline__ void row(float (&acc)[8], float& hsum, uint32_t raw, uint32_t w) {
+    const uint32_t v0 = ((w << 6) & 0x03C003C0u) | 0x48004800u;   // outputs 0, 4
+    const uint32_t v1 = ((w << 2) & 0x03C003C0u) | 0x48004800u;   // 1, 5
+    const uint32_t v2 = ((w >> 2) & 0x03C003C0u) | 0x48004800u;   // 2, 6
+    const uint32_t v3 = ((w >> 6) & 0x03C003C0u) | 0x48004800u;   // 3, 7
+    asm("{\n .reg .b16 a0, a1, a2, a3, a4, a5, a6, a7, hh, one;\n"
+        " mov.b32 {a0, a4}, %10;\n mov.b32 {a1, a5}, %11;\n mov.b32 {a2, a6}, %12;\n mov.b32 {a3, a7}, %13;\n"
+        " mov.b32 {hh, _}, %9;\n mov.b16 one, 0x3C00;\n"
+        " fma.rn.f32.f16 %0, hh, a0, %0;\n fma.rn.f32.f16 %1, hh, a1, %1;\n"
+        " fma.rn.f32.f16 %2, hh, a2, %2;\n fma.rn.f32.f16 %3, hh, a3, %3;\n"
+        " fma.rn.f32.f16 %4, hh, a4, %4;\n fma.rn.f32.f16 %5, hh, a5, %5;\n"
+        " fma.rn.f32.f16 %6, hh, a6, %6;\n fma.rn.f32.f16 %7, hh, a7, %7;\n"
+        " fma.rn.f32.f16 %8, hh, one, %8;\n}"
+        : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3]), "+f"(acc[4]), "+f"(acc[5]), "+f"(acc[6]),
+          "+f"(acc[7]), "+f"(hsum)
+        : "r"(raw), "r"(v0), "r"(v1), "r"(v2), "r"(v3));
+  }
+  static __device__ __forceinline__ bool live(uint32_t raw) { return (raw & 0x7FFFu) != 0u; }
+};
+
+template <>
+struct RowMath<float> {
+  template <int N>
+  static __device__ __forceinline__ float q8(uint32_t w) {   // 8 + q_N / 2 as fp32
+    constexpr int sh = 19 - 4 * N;
+    const uint32_t m = (sh >= 0) ? (w << (sh >= 0 ? sh : 0)) : (w >> (sh < 0 ? -sh : 0));
+    return __uint_as_float((m & 0x00780000u) | 0x41000000u);
+  }
+  static __device__ __forceinline__ void row(float (&acc)[8], float& hsum, uint32_t raw, uint32_t w) {
+    const float h = __uint_as_float(raw);
+    acc[0] = fmaf(h, q8<0>(w), acc[0]);
+    acc[1] = fmaf(h, q8<1>(w), acc[1]);
+    acc[2] = fmaf(h, q8<2>(w), acc[2]);
+    acc[3] = fmaf(h, q8<3>(w), acc[3]);
+    acc[4] = fmaf(h, q8<4>(w), acc[4]);
+    acc[5] = fmaf(h, q8<5>(w), acc[5]);
+    acc[6] = fmaf(h, q8<6>(w), acc[6]);
+    acc[7] = fmaf(h, q8<7>(w), acc[7]);
+    hsum += h;
+  }
+  static __device__ __forceinline__ bool live(uint32_t raw) { return (raw & 0x7FFFFFFFu) != 0u; }
+};
+
+// ---- memory helpers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t evict_normal_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
 }
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -172,50 +195,24 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
   asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}"
                ::"r"(bar), "r"(bytes) : "memory");
 }
+// try_wait suspends the thread until the phase completes or ~1 us passes (no hot spin).
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000;\n selp.u32 %0, 1, 0, p;\n}"
                : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
   return ok != 0;
+}
+// One TMA bulk copy global -> this CTA's shared memory, completing on `bar` (L2 hint).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
 }
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait for the phase with `parity`: false after ~2 s.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity))
-    if (global_ns() - t0 > 2000000000ull) return false;
-  return true;
-}
-__device__ __forceinline__ uint64_t evict_first_policy() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-// One TMA bulk copy global -> this CTA's shared memory, completing on `bar`.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint32_t bar,
-                                         uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
-}
-
-// 16 bytes global -> this CTA's shared memory on the load/store path (cp.async, L2 hint),
-// beside the TMA unit: the two paths issue in parallel.
-__device__ __forceinline__ void cp16(void* dst, const void* src, uint64_t pol) {
-  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;"
-               ::"r"(smem_u32(dst)), "l"(src), "l"(pol) : "memory");
-}
-// One arrival on `bar` once every cp.async this thread issued before it has landed (the
-// barrier's expected count includes one such arrival per thread).
-__device__ __forceinline__ void cp_arrive(uint32_t bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-
 // ---- distributed shared memory helpers
 // The address of this CTA's shared-memory location `a` in cluster CTA `r`.
 __device__ __forceinline__ uint32_t mapa_u32(uint32_t a, uint32_t r) {
@@ -230,9 +227,17 @@ __device__ __forceinline__ void st_async_f32(uint32_t addr, float v, uint32_t re
 }
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, 1000;\n selp.u32 %0, 1, 0, p;\n}"
                : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
   return ok != 0;
+}
+// Bounded wait for the phase with `parity`: false after ~2 s.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > 2000000000ull) return false;
+  return true;
 }
 // Bounded wait (cluster-scope acquire) for the phase with `parity`: false after ~2 s.
 __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint32_t bar, uint32_t parity) {
@@ -243,14 +248,59 @@ __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint32_t bar, uint32_t
   return true;
 }
 
-template <typename HT, typename ST, typename YT, int C>
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>::THREADS)
+// 16 bytes global -> this CTA's shared memory on the load/store path (cp.async, L2 hint).
+__device__ __forceinline__ void cp16(uint32_t dst, const void* src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_commit_wait() {
+  asm volatile("cp.async.commit_group;\n cp.async.wait_all;" ::: "memory");
+}
+
+// Starts the copies of live-row entries [t0, t0 + RG) of a group into its stage
+// ([RG][NWC] words): 8 lanes per row, 16 bytes a lane, 4 rows per warp instruction -- the memory
+// system's cost is per instruction, not per byte, so a row takes a quarter of an instruction.
+// Lane e holds the row offset (row * NW, in words) of list entry e in off0 and of entry 32 + e
+// in off1; `rows` points at word w0 of the group's first row.
+template <int RG, int NWC>
+__device__ __forceinline__ void stage_rows(uint32_t stage, const uint32_t* rows, int t0, int n, int off0, int off1,
+                                           int nwc, int lane, uint64_t pol) {
+  const int piece = lane & 7, sub = lane >> 3;
+#pragma unroll
+  for (int k = 0; k < RG / 4; ++k) {
+    const int e = t0 + 4 * k + sub;
+    if (t0 + 4 * k < n) {                         // warp-uniform
+      const int off = __shfl_sync(0xffffffffu, (t0 + 4 * k < 32) ? off0 : off1, e & 31);
+      if (e < n && 4 * piece < nwc)
+        cp16(stage + static_cast<uint32_t>(((4 * k + sub) * NWC + 4 * piece) * 4), rows + off + 4 * piece, pol);
+    }
+  }
+}
+
+// Accumulates the staged rows of entries [t0, t0 + RG), in list (ascending) order; lane e holds
+// the raw h bits of entry e in hb0 and of entry 32 + e in hb1.
+template <typename HT, int RG, int NWC>
+__device__ __forceinline__ void consume_rows(const uint32_t* stage, int t0, int n, uint32_t hb0, uint32_t hb1,
+                                             int lane, float (&acc)[8], float& hsum) {
+#pragma unroll
+  for (int t = 0; t < RG; ++t) {
+    const int e = t0 + t;
+    if (e < n) {                                  // warp-uniform
+      const uint32_t hv = __shfl_sync(0xffffffffu, (t0 + t < 32) ? hb0 : hb1, e & 31);
+      RowMath<HT>::row(acc, hsum, hv, stage[t * NWC + lane]);
+    }
+  }
+}
+
+template <typename HT, typename ST, typename YT, int C, int RG, int MINB>
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MINB)
     sparse_down_decode_kernel(const DecodeParams p) {
-  using Cfg = DecodeCfg<C>;
-  constexpr int NWC = Cfg::NWC, NGL = Cfg::NGL, THREADS = Cfg::THREADS, WARPS = Cfg::WARPS;
-  constexpr int HPV = 16 / sizeof(HT);           // h values per 16-byte load
+  using Smem = DecodeSmem<C, RG>;
+  constexpr int NWC = C / 8;                      // words of one row in a chunk
+  constexpr int THREADS = kNGL * 32;
+  static_assert(NWC <= 32 && NWC % 4 == 0, "a chunk row is 4..32 words, 16-byte pieces");
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  DecodeSmem<C>& S = *reinterpret_cast<DecodeSmem<C>*>(smem_raw);
+  Smem& S = *reinterpret_cast<Smem*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -258,35 +308,25 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
   const int ch = blockIdx.x / kCluster;
   const int b = blockIdx.y;
   const int w0 = ch * NWC;                        // first word of this chunk
-  const int nwc = min(NWC, p.NW - w0);            // words of this chunk (tail chunk may be short)
+  const int nwc = min(NWC, p.NW - w0);            // words of this chunk (the tail chunk may be short)
+  const bool active = lane < nwc;
   const int GF = p.F / kGS;
   const int g_lo = static_cast<int>((static_cast<long long>(rank) * p.GT) / kCluster);
   const int g_hi = static_cast<int>((static_cast<long long>(rank + 1) * p.GT) / kCluster);
-  // A group lane is a warp and its lane wp owns word wp of the chunk: the lanes of a warp
-  // walk the same rows, so the row loop never diverges (C < 256 leaves lanes idle).
-  const int wp = lane;                            // word of the chunk this thread owns
-  const int gl = warp;                            // group lane
-  const bool lane_used = wp < NWC;
-  const bool active = wp < nwc;
-  uint32_t* ring = reinterpret_cast<uint32_t*>(smem_raw + ring_offset<C>());
-  const int SBR = p.SBR, nring = p.nring;
-  const uint32_t bar0 = smem_u32(&S.bars[0]);     // slot k's mbarrier: bar0 + 8*k
   const uint32_t rbar = smem_u32(&S.rbar);
-  const uint32_t row_bytes = static_cast<uint32_t>(nwc) * 4;
   constexpr int per = C / kCluster;               // outputs of the chunk each CTA finishes
-  uint32_t phases = 0;                            // bit k: the parity slot k waits for next
   const uint64_t pol = evict_first_policy();
+  const uint64_t hpol = evict_normal_policy();
 
   if (tid == 0) {
-    // a slot's phase: the arrival carrying its TMA bytes + one cp.async arrival per thread
-    for (int k = 0; k < kMaxSlots; ++k) mbar_init(bar0 + 8u * k, 1 + THREADS);
     mbar_init(rbar, 1);
+    for (int w = 0; w < kNGL; ++w) mbar_init(smem_u32(&S.mbar[w]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // the 8 slices of C/8 partials that the cluster's CTAs push here complete this phase
     mbar_arrive_expect_tx(rbar, static_cast<uint32_t>(sizeof(float) * C));
   }
   __syncthreads();
-  // the handshake that makes every CTA's mbarriers visible before any push (waited in 6.)
+  // the handshake that makes every CTA's mbarrier visible before any push (waited below)
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   // Programmatic dependent launch: let the next kernel in the stream start its launch
   // now, and wait for the previous one (which produces h / sel / gains) before reading.
@@ -296,226 +336,184 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
   float out[8];
 #pragma unroll
   for (int n = 0; n < 8; ++n) out[n] = 0.f;
+  const uint32_t wbar = smem_u32(&S.mbar[warp]);
+  uint32_t wphase = 0;
 
-  for (int gb0 = g_lo; gb0 < g_hi; gb0 += kGB) {
-    const int ng = min(kGB, g_hi - gb0);
-    // the previous batch's shared-memory reads come before this batch's bulk copies
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    // ---- 1. h columns [64*gb0, 64*(gb0+ng)) of row b, the groups' expert ids and gains
+  const int64_t hrow = static_cast<int64_t>(b) * p.NR;
+  // Round r: this warp (group lane `warp`) takes groups r0 + warp and r0 + warp + 16.
+  for (int r0 = g_lo; r0 < g_hi; r0 += 2 * kNGL) {
+    // ---- 1. the round's 32 groups' h values into shared memory (16-byte pieces, spread over
+    //         the CTA's threads) and -- one warp for the whole CTA -- their expert ids and gains
     {
-      const HT* hrow = reinterpret_cast<const HT*>(p.h) + static_cast<int64_t>(b) * p.NR +
-                       static_cast<int64_t>(gb0) * kGS;
-      for (int v = tid; v < ng * kGS / HPV; v += THREADS) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(hrow) + v);
-        const HT* e = reinterpret_cast<const HT*>(&raw);
-        float f[HPV];
-#pragma unroll
-        for (int i = 0; i < HPV; ++i) f[i] = hsd::to_f32<HT>(e[i]);
-#pragma unroll
-        for (int i = 0; i < HPV; i += 4)
-          *reinterpret_cast<float4*>(&S.hs[v * HPV + i]) = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
+      constexpr int PIECES = 4 * static_cast<int>(sizeof(HT));   // 16-byte pieces of one group's h
+      const int gi = tid / PIECES, part = tid % PIECES;
+      if (gi < 2 * kNGL && r0 + gi < g_hi)
+        cp16(smem_u32(&S.hs[gi][0]) + 16u * part,
+             reinterpret_cast<const unsigned char*>(p.h) + (hrow + static_cast<int64_t>(r0 + gi) * kGS) * sizeof(HT) + 16 * part,
+             hpol);
+    }
+    if (warp == 0) {
+      const int g = r0 + lane;
+      int src = -2;
+      float gain = 0.f;
+      if (g < g_hi) {
+        const bool routed = g < p.topk * GF;
+        const int slot = routed ? g / GF : p.topk;
+        src = routed ? __ldg(p.sel + static_cast<int64_t>(b) * p.topk + slot) : -1;
+        gain = __ldg(p.gains + static_cast<int64_t>(b) * (p.topk + 1) + slot);
+        if (routed && (src < 0 || src >= p.E)) {
+          hsd_flag_decode(HSD_ERR_INDEX);
+          src = -2;
+        }
       }
-      if (tid < ng) {
-        const int G = gb0 + tid;
-        int slot, loc, src;
-        if (G < p.topk * GF) {
-          slot = G / GF;
-          loc = G - slot * GF;
-          src = __ldg(p.sel + static_cast<int64_t>(b) * p.topk + slot);
-          if (src < 0 || src >= p.E) {
-            hsd_flag_decode(HSD_ERR_INDEX);
-            src = -2;
+      S.gsrc[lane] = src;
+      S.ggain[lane] = gain;
+    }
+    cp_commit_wait();
+    __syncthreads();
+    // ---- 2. per group: the live mask, the compacted list of live rows (entry e: row j and its
+    //         h, held by lane e % 32), the copies of the first RG live rows into the group's
+    //         stage, then the scale / bias chunks -- all in flight together
+    const uint32_t* rows[2];
+    float gain[2];
+    int n[2], off0[2], off1[2], srcs[2];
+    uint32_t hv0[2], hv1[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int gi = warp + kNGL * i;              // the group's index in this round
+      const int g = r0 + gi;
+      const int src = S.gsrc[gi];
+      srcs[i] = src;
+      const bool valid = src != -2;                 // (g >= g_hi is stored as -2)
+      gain[i] = S.ggain[gi];
+      // lane l holds entries 2l (h0) and 2l+1 (h1); even / odd live masks, bit l = entry 2l(+1)
+      uint32_t h0, h1;
+      if constexpr (sizeof(HT) == 4) {
+        const uint2 r = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint32_t*>(&S.hs[gi][0]) + 2 * lane);
+        h0 = r.x;
+        h1 = r.y;
+      } else {
+        const uint32_t r = reinterpret_cast<const uint32_t*>(&S.hs[gi][0])[lane];
+        h0 = r & 0xffffu;
+        h1 = r >> 16;
+      }
+      const unsigned me = p.all_rows ? (valid ? 0xffffffffu : 0u) : __ballot_sync(0xffffffffu, valid && RowMath<HT>::live(h0));
+      const unsigned mo = p.all_rows ? (valid ? 0xffffffffu : 0u) : __ballot_sync(0xffffffffu, valid && RowMath<HT>::live(h1));
+      n[i] = __popc(me) + __popc(mo);
+      const int loc = valid ? ((src >= 0) ? g - (g / GF) * GF : g - p.topk * GF) : 0;
+      const int64_t row0 = (src >= 0) ? static_cast<int64_t>(src) * p.F + static_cast<int64_t>(loc) * kGS
+                                      : static_cast<int64_t>(loc) * kGS;
+      rows[i] = ((src >= 0) ? p.pw : p.spw) + row0 * p.NW + w0;          // word w0 of the group's row 0
+      // compaction: row 2l+par goes to entry (live rows below it) = popc(me below l(+1)) + popc(mo below l)
+      const unsigned below = (1u << lane) - 1u;     // lanes below this one
+      const int eo = __popc(mo & below);
+      const int ee = __popc(me & below) + eo;      // entry of row 2l
+      short* cj = S.cj[warp][i];
+      uint32_t* ch_ = S.ch[warp][i];
+      if ((me >> lane) & 1u) {
+        cj[ee] = static_cast<short>(2 * lane);
+        ch_[ee] = h0;
+      }
+      if ((mo >> lane) & 1u) {
+        const int e1 = ee + static_cast<int>((me >> lane) & 1u);          // entry of row 2l+1
+        cj[e1] = static_cast<short>(2 * lane + 1);
+        ch_[e1] = h1;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      off0[i] = (lane < n[i]) ? S.cj[warp][i][lane] * p.NW : 0;
+      off1[i] = (lane + 32 < n[i]) ? S.cj[warp][i][lane + 32] * p.NW : 0;
+      hv0[i] = (lane < n[i]) ? S.ch[warp][i][lane] : 0u;
+      hv1[i] = (lane + 32 < n[i]) ? S.ch[warp][i][lane + 32] : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+      stage_rows<RG, NWC>(smem_u32(&S.stage[warp][i][0][0]), rows[i], 0, n[i], off0[i], off1[i], nwc, lane, pol);
+    // the live groups' scale and bias chunks: TMA bulk copies (nwc*16 bytes each) into the
+    // warp's area, completing on the warp's mbarrier, beside the load/store path the rows use
+    const uint32_t mbytes = static_cast<uint32_t>(nwc) * 16;
+    const bool ml0 = p.loadsc && n[0] != 0, ml1 = p.loadsc && n[1] != 0;
+    const uint32_t wbytes = ((ml0 ? 1u : 0u) + (ml1 ? 1u : 0u)) * 2 * mbytes;
+    if (wbytes != 0 && lane < 4) {
+      const int i = lane >> 1, sb = lane & 1;
+      if (lane == 0) mbar_arrive_expect_tx(wbar, wbytes);
+      __syncwarp(0xfu);
+      if (i == 0 ? ml0 : ml1) {
+        const int src = i == 0 ? srcs[0] : srcs[1];
+        const int g = r0 + warp + kNGL * i;
+        const int loc = (src >= 0) ? g - (g / GF) * GF : g - p.topk * GF;
+        const int64_t mrow = (src >= 0) ? static_cast<int64_t>(src) * GF + loc : loc;
+        const uint16_t* base = (src >= 0) ? (sb ? p.pb : p.ps) : (sb ? p.spb : p.sps);
+        bulk_g2s(&S.meta[warp][i][sb][0], base + mrow * p.D + static_cast<int64_t>(w0) * 8, mbytes, wbar, pol);
+      }
+    }
+    cp_commit_wait();
+    __syncwarp();
+    if (wbytes != 0) {                           // warp-uniform
+      if (!mbar_wait_bounded(wbar, wphase)) {
+        if (lane == 0) hsd_flag_decode(HSD_ERR_TIMEOUT);
+        mbar_wait_bounded(wbar, wphase);         // once more for the copies still in flight
+      }
+      wphase ^= 1u;
+    }
+    // ---- 3. accumulate and fold, the lane's groups in ascending order
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      if (n[i] == 0) continue;                    // warp-uniform
+      float acc[8], hsum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+      consume_rows<HT, RG, NWC>(&S.stage[warp][i][0][0], 0, n[i], hv0[i], hv1[i], lane, acc, hsum);
+      for (int t0 = RG; t0 < n[i]; t0 += RG) {     // groups with more than RG live rows
+        __syncwarp();
+        stage_rows<RG, NWC>(smem_u32(&S.stage[warp][i][0][0]), rows[i], t0, n[i], off0[i], off1[i], nwc, lane, pol);
+        cp_commit_wait();
+        __syncwarp();
+        consume_rows<HT, RG, NWC>(&S.stage[warp][i][0][0], t0, n[i], hv0[i], hv1[i], lane, acc, hsum);
+      }
+      const float h8 = 8.f * hsum;               // exact
+      if (active) {
+        if (p.loadsc) {
+          const uint4 s4 = *reinterpret_cast<const uint4*>(&S.meta[warp][i][0][lane * 8]);
+          const uint4 b4 = *reinterpret_cast<const uint4*>(&S.meta[warp][i][1][lane * 8]);
+          const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
+          const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float sc = hsd::bits16_to_f32<ST>(static_cast<uint16_t>(sw[k >> 1] >> (16 * (k & 1))));
+            const float bi = hsd::bits16_to_f32<ST>(static_cast<uint16_t>(bw[k >> 1] >> (16 * (k & 1))));
+            out[k] = fmaf(gain[i], fmaf(2.f * sc, acc[k] - h8, bi * hsum), out[k]);
           }
         } else {
-          slot = p.topk;
-          loc = G - p.topk * GF;
-          src = -1;
-        }
-        S.gsrc[tid] = src;
-        S.gloc[tid] = loc;
-        S.ggain[tid] = __ldg(p.gains + static_cast<int64_t>(b) * (p.topk + 1) + slot);
-      }
-    }
-    __syncthreads();
-    // ---- 2. live masks (one warp per group)
-    for (int gi = warp; gi < ng; gi += WARPS) {
-      const bool valid = S.gsrc[gi] != -2;
-      const float v0 = valid ? S.hs[gi * kGS + lane] : 0.f;
-      const float v1 = valid ? S.hs[gi * kGS + 32 + lane] : 0.f;
-      const unsigned long long m = p.all_rows ? ballot64(valid, valid) : ballot64(v0 != 0.f, v1 != 0.f);
-      if (lane == 0) {
-        S.gmask[gi] = m;
-        S.gcnt[gi] = __popcll(m);
-      }
-      if (m != 0ull && p.loadsc && lane < nwc) {   // a live group's scale and bias chunks: 16 bytes a lane
-        const int src = S.gsrc[gi];
-        const int64_t grow = (src >= 0) ? static_cast<int64_t>(src) * GF + S.gloc[gi] : S.gloc[gi];
-        const int64_t go = grow * p.D + static_cast<int64_t>(w0) * 8 + lane * 8;
-        cp16(S.meta_s + gi * C + lane * 8, ((src >= 0) ? p.ps : p.sps) + go, pol);   // complete on slot 0
-        cp16(S.meta_b + gi * C + lane * 8, ((src >= 0) ? p.pb : p.spb) + go, pol);
-      }
-    }
-    __syncthreads();
-    // ---- 3. the counts' exclusive scan and the sub-batch cut (every warp, redundantly),
-    //         the compaction and the row copies of the first nring sub-batches
-    int nsb = 0;
-    {
-      const int c = (lane < ng) ? S.gcnt[lane] : 0;
-      int x = c;
 #pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, d);
-        if (lane >= d) x += y;
-      }
-      const int goff_lane = x - c;                 // group `lane`'s rows: [goff_lane, x)
-      const int nrows = __shfl_sync(0xffffffffu, x, 31);
-      // greedy cut into sub-batches of whole groups of at most SBR rows (a group never
-      // straddles two, so it is always folded in one piece: a group's sum is the same
-      // sequence of fp32 operations whatever the other groups' live counts). Lane k ends
-      // holding sub-batch k's first row (my_sbeg) and last row + 1 (my_send); my_sb is the
-      // sub-batch of group `lane`.
-      int my_sbeg = 0, my_sb = 0;
-      for (int start = 0; start < nrows; ++nsb) {
-        const unsigned cand = (lane < ng && x > start && x - start <= SBR) ? static_cast<unsigned>(x) : 0u;
-        const int nxt = static_cast<int>(__reduce_max_sync(0xffffffffu, cand));
-        if (lane == nsb) my_sbeg = start;
-        if (lane < ng && goff_lane >= start && goff_lane < nxt) my_sb = nsb;
-        start = nxt;
-      }
-      if (lane == nsb) my_sbeg = nrows;
-      const int next_beg = __shfl_down_sync(0xffffffffu, my_sbeg, 1);
-      const int my_send = (lane + 1 >= nsb) ? nrows : next_beg;
-      if (warp == 0) {
-        if (lane < ng) S.goff[lane] = goff_lane;
-        if (lane == 0) S.goff[ng] = nrows;
-        if (lane < nsb) S.sbeg[lane] = my_sbeg;
-        if (lane == 0) S.sbeg[nsb] = nrows;
-        // each in-flight sub-batch's TMA byte count (its rows), registered once with its
-        // slot's arrival (copies already issued may complete first: the phase cannot end
-        // before the arrivals); the cp.async scale/bias chunks complete on slot 0 through
-        // the threads' cp.async arrivals
-        if (lane < min(nsb, nring))
-          mbar_arrive_expect_tx(bar0 + 8u * lane, static_cast<uint32_t>(my_send - my_sbeg) * row_bytes);
-      }
-      for (int gi = warp; gi < ng; gi += WARPS) {
-        const unsigned long long m = S.gmask[gi];
-        const int base = __shfl_sync(0xffffffffu, goff_lane, gi);
-        const int sb = __shfl_sync(0xffffffffu, my_sb, gi);
-        const int sb_first = __shfl_sync(0xffffffffu, my_sbeg, sb & 31);
-        const int src = S.gsrc[gi];
-        const int64_t rowbase = (src >= 0) ? (static_cast<int64_t>(src) * p.F + static_cast<int64_t>(S.gloc[gi]) * kGS)
-                                           : static_cast<int64_t>(S.gloc[gi]) * kGS;
-        const uint32_t* wbase = (src >= 0) ? p.pw : p.spw;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int j = lane + 32 * half;
-          if ((m >> j) & 1ull) {
-            const int idx = base + live_prefix(m, j);
-            S.rows[idx] = static_cast<uint16_t>((gi << 6) | j);
-            S.hrow[idx] = S.hs[gi * kGS + j];
-            if (sb < nring) {
-              uint32_t* dst = ring + static_cast<size_t>(sb * SBR + idx - sb_first) * NWC;
-              const uint32_t* src = wbase + (rowbase + j) * p.NW + w0;
-              bulk_g2s(dst, src, row_bytes, bar0 + 8u * sb, pol);
-            }
-          }
+          for (int k = 0; k < 8; ++k) out[k] = fmaf(gain[i], fmaf(2.f, acc[k] - h8, hsum), out[k]);
         }
       }
-      // one cp.async arrival per thread on every slot in flight (the scale/bias pieces land
-      // with slot 0's phase)
-      for (int k = 0; k < min(nsb, nring); ++k) cp_arrive(bar0 + 8u * k);
     }
-    __syncthreads();
-
-    // ---- 4. per sub-batch, as its slot's copies land: accumulate from shared memory, then
-    //         refill the slot with the sub-batch nring places later
-    for (int k = 0; k < nsb; ++k) {
-      const int r0 = S.sbeg[k], r1 = S.sbeg[k + 1];
-      const int sk = k % nring;
-      const uint32_t bk = bar0 + 8u * sk;
-      const uint32_t* stage = ring + static_cast<size_t>(sk) * SBR * NWC;
-      if (!mbar_wait_bounded(bk, (phases >> sk) & 1u)) {
-        if (tid == 0) hsd_flag_decode(HSD_ERR_TIMEOUT);
-        mbar_wait_bounded(bk, (phases >> sk) & 1u);   // once more for the copies still in flight
-      }
-      phases ^= 1u << sk;
-      if (active) {
-        for (int gi = gl; gi < ng; gi += NGL) {
-          const int j0 = max(S.goff[gi], r0), j1 = min(S.goff[gi + 1], r1);
-          if (j0 >= j1) continue;
-          float acc[8], hsum = 0.f;
-#pragma unroll
-          for (int n = 0; n < 8; ++n) acc[n] = 0.f;
-          for (int r = j0; r < j1; ++r) {
-            const float hv = S.hrow[r];
-            const uint32_t q = stage[(r - r0) * NWC + wp];
-            hsum += hv;
-            ffma2(acc[0], acc[1], hv, nib_unit<0>(q), nib_unit<1>(q));
-            ffma2(acc[2], acc[3], hv, nib_unit<2>(q), nib_unit<3>(q));
-            ffma2(acc[4], acc[5], hv, nib_unit<4>(q), nib_unit<5>(q));
-            ffma2(acc[6], acc[7], hv, nib_unit<6>(q), nib_unit<7>(q));
-          }
-          const float g = S.ggain[gi];
-          if (p.loadsc) {
-            const uint4 s4 = *reinterpret_cast<const uint4*>(&S.meta_s[gi * C + wp * 8]);
-            const uint4 b4 = *reinterpret_cast<const uint4*>(&S.meta_b[gi * C + wp * 8]);
-            const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
-            const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-            for (int n = 0; n < 8; ++n) {
-              const float sc = hsd::bits16_to_f32<ST>(static_cast<uint16_t>(sw[n >> 1] >> (16 * (n & 1))));
-              const float bi = hsd::bits16_to_f32<ST>(static_cast<uint16_t>(bw[n >> 1] >> (16 * (n & 1))));
-              out[n] = fmaf(g, fmaf(16.f * sc, acc[n] - hsum, bi * hsum), out[n]);
-            }
-          } else {
-#pragma unroll
-            for (int n = 0; n < 8; ++n) out[n] = fmaf(g, fmaf(16.f, acc[n] - hsum, hsum), out[n]);
-          }
-        }
-      }
-      if (k + nring < nsb) {                     // refill slot sk (every thread is done with it)
-        __syncthreads();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        const int q0 = S.sbeg[k + nring], qn = S.sbeg[k + nring + 1] - q0;
-        if (tid == 0) mbar_arrive_expect_tx(bk, static_cast<uint32_t>(qn) * row_bytes);
-        for (int r = tid; r < qn; r += THREADS) {
-          const int code = S.rows[q0 + r];
-          const int gi = code >> 6, j = code & 63;
-          const int src = S.gsrc[gi];
-          const int64_t neuron = static_cast<int64_t>(S.gloc[gi]) * kGS + j;
-          const uint32_t* g = (src >= 0) ? p.pw + (static_cast<int64_t>(src) * p.F + neuron) * p.NW
-                                         : p.spw + neuron * p.NW;
-          uint32_t* dst = ring + (static_cast<size_t>(sk) * SBR + r) * NWC;
-          bulk_g2s(dst, g + w0, row_bytes, bk, pol);
-        }
-        cp_arrive(bk);
-      }
-    }
-    __syncthreads();                             // the ring, meta and hs are rewritten next
+    __syncthreads();                             // the round's shared tables are rewritten next
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // before the next round's bulk copies
   }
 
-  // ---- 5. reduce the group lanes (fixed order) into S.part, reusing the ring
-  float* red = reinterpret_cast<float*>(ring);   // [NGL][C] fp32 (the host keeps ring >= MIN_RB rows)
-  if (lane_used) {
-    *reinterpret_cast<float4*>(&red[gl * C + wp * 8]) = make_float4(out[0], out[1], out[2], out[3]);
-    *reinterpret_cast<float4*>(&red[gl * C + wp * 8 + 4]) = make_float4(out[4], out[5], out[6], out[7]);
+  // ---- 4. the 16 group lanes, reduced in a fixed order into S.part
+  if (lane < NWC) {
+    *reinterpret_cast<float4*>(&S.red[warp][lane * 8]) = make_float4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<float4*>(&S.red[warp][lane * 8 + 4]) = make_float4(out[4], out[5], out[6], out[7]);
   }
   __syncthreads();
-  {                                              // 4 partial sums per output, then their sum
-    constexpr int NP = 4, PER = (NGL + NP - 1) / NP;
-    float* red2 = S.hs;                          // [NP][C] (hs is free now)
-    for (int t = tid; t < NP * C; t += THREADS) {
-      const int o = t % C, q = t / C;
+  for (int o = tid; o < C; o += THREADS) {       // 4 partial sums of 4 lanes, then their sum
+    float q4[4];
+#pragma unroll
+    for (int qd = 0; qd < 4; ++qd) {
       float a = 0.f;
 #pragma unroll
-      for (int l = q * PER; l < min(NGL, (q + 1) * PER); ++l) a += red[l * C + o];
-      red2[q * C + o] = a;
+      for (int L = 4 * qd; L < 4 * qd + 4; ++L) a += S.red[L][o];
+      q4[qd] = a;
     }
-    __syncthreads();
-    for (int o = tid; o < C; o += THREADS)
-      S.part[o] = (red2[o] + red2[C + o]) + (red2[2 * C + o] + red2[3 * C + o]);
+    S.part[o] = (q4[0] + q4[1]) + (q4[2] + q4[3]);
   }
-  // ---- 6. the cluster's 8 partials: slice r of every CTA's chunk goes to CTA r (st.async,
+  // ---- 5. the cluster's 8 partials: slice r of every CTA's chunk goes to CTA r (st.async,
   //         completing on CTA r's rbar), which sums the 8 slices in rank order
   __syncthreads();
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // every rbar is initialised
@@ -543,7 +541,27 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(DecodeCfg<C>:
   // pushed to it have landed, so no closing cluster barrier is needed.
 }
 
-// ---- active-index sets, the same ballot compaction per (token, slot)
+// ---- active-index sets (hsd/decode.py:86-101): per (token, slot) the ascending nonzero
+//      indices, by warp ballots and prefix popcounts
+
+// Live mask of 64 h values (entry j read by lane j % 32) with two ballots.
+__device__ __forceinline__ unsigned long long ballot64(bool nz0, bool nz1) {
+  const unsigned lo = __ballot_sync(0xffffffffu, nz0);
+  const unsigned hi = __ballot_sync(0xffffffffu, nz1);
+  return (static_cast<unsigned long long>(hi) << 32) | lo;
+}
+
+// Index of this lane's entry (j = lane or lane + 32) among the live entries of mask.
+__device__ __forceinline__ int live_prefix(unsigned long long mask, int j) {
+  const unsigned long long below = (j == 0) ? 0ull : (mask & ((1ull << j) - 1ull));
+  return __popcll(below);
+}
+
+template <typename HT>
+__device__ __forceinline__ float load_h(const void* h, int64_t idx) {
+  return hsd::to_f32<HT>(reinterpret_cast<const HT*>(h)[idx]);
+}
+
 constexpr int kLiveThreads = 256;
 constexpr int kWarps = kLiveThreads / 32;
 
@@ -586,47 +604,37 @@ __global__ void __launch_bounds__(kLiveThreads) live_rows_kernel(const void* h, 
   if (threadIdx.x == 0) count[static_cast<int64_t>(b) * (topk + 1) + slot] = base_s;
 }
 
-// The staging ring per launch (measured on B200, 23 layers, z = 0.90, 192-output chunks): one
-// token stages up to 1024 rows in one slot (one CTA per SM: a token's CTAs never share an
-// SM); larger batches stage 256 rows in one slot (several CTAs share an SM, so a verify step
-// of 3 rows runs in one wave: 24 -> 14 us a layer at B = 3, 48 -> 33 us at B = 8). Splitting the same rows into 2-8 pipelined slots measured slower at every batch
-// size: the copies of a sub-batch land together, and each extra wait costs more than the
-// overlap gains. HSD_DECODE_SBR / HSD_DECODE_RING force the slot rows / slot count.
-inline void ring_choice(int B, int min_rb, int* sbr, int* nring) {
-  static const int forced_sbr = [] { const char* e = getenv("HSD_DECODE_SBR"); return e ? atoi(e) : 0; }();
-  static const int forced_ring = [] { const char* e = getenv("HSD_DECODE_RING"); return e ? atoi(e) : 0; }();
-  *sbr = B == 1 ? 1024 : 256;
-  *nring = 1;
-  if (forced_sbr >= 64 && forced_sbr <= 1024) *sbr = forced_sbr;
-  if (forced_ring >= 1 && forced_ring <= kMaxSlots) *nring = forced_ring;
-  while (*sbr * *nring < min_rb || *sbr * *nring > 1024) {
-    if (*sbr * *nring < min_rb) ++*nring; else --*nring;
-    if (*nring > kMaxSlots) { *nring = kMaxSlots; *sbr *= 2; }
-    if (*nring < 1) { *nring = 1; *sbr /= 2; }
-  }
+// Launch shape. Chunks of C = 256 outputs (a chunk row is one warp's 32 words; at D = 2688
+// a token is 10 full chunks and a half-width tail, 88 CTAs per token) and 16 warps per CTA.
+// One token loads up to 16 live rows of a group per round trip (112 registers, one CTA per
+// SM); a batch up to 8 (64 registers: two CTAs per SM, so a 3-row verify step runs in one
+// wave). HSD_DECODE_RG (8, 16) and HSD_DECODE_SMEM (dynamic shared memory in bytes, to limit
+// the CTAs per SM) override the choice; HSD_DECODE_CHUNK (128, 192, 256) the chunk width.
+// None of them changes a token's arithmetic.
+int env_int(const char* name) {
+  const char* e = getenv(name);
+  return e ? atoi(e) : 0;
 }
 
-template <typename HT, typename ST, typename YT, int C>
-int launch_decode(DecodeParams p, cudaStream_t st) {
-  using Cfg = DecodeCfg<C>;
-  auto kern = sparse_down_decode_kernel<HT, ST, YT, C>;
-  static_assert(Cfg::MIN_RB <= Cfg::MAX_RB, "ring bounds");
-  ring_choice(p.B, Cfg::MIN_RB, &p.SBR, &p.nring);
-  const size_t smem = ring_offset<C>() + sizeof(uint32_t) * Cfg::NWC * p.SBR * p.nring;
-  const size_t smem_max = ring_offset<C>() + sizeof(uint32_t) * Cfg::NWC * Cfg::MAX_RB;
+template <typename HT, typename ST, typename YT, int C, int RG, int MINB>
+int launch_decode(const DecodeParams& p, cudaStream_t st) {
+  auto kern = sparse_down_decode_kernel<HT, ST, YT, C, RG, MINB>;
+  static const int forced_smem = env_int("HSD_DECODE_SMEM");
+  size_t smem = sizeof(DecodeSmem<C, RG>);
+  if (forced_smem > 0 && static_cast<size_t>(forced_smem) > smem) smem = static_cast<size_t>(forced_smem);
+  if (smem > 227 * 1024) smem = 227 * 1024;
   static int configured_device = -1;           // the attribute is set once per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem_max));
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return hsd::check_cuda(e, "hsd_sparse_down_decode: smem attribute");
     configured_device = dev;
   }
-  const int nch = (p.NW + Cfg::NWC - 1) / Cfg::NWC;
+  const int nch = (p.NW + C / 8 - 1) / (C / 8);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nch * kCluster, p.B);
-  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.blockDim = dim3(kNGL * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -637,29 +645,23 @@ int launch_decode(DecodeParams p, cudaStream_t st) {
   return hsd::check_cuda(cudaLaunchKernelEx(&cfg, kern, p), "hsd_sparse_down_decode launch");
 }
 
-// Output chunk width (outputs per cluster): 256 at every batch size -- a chunk row is one
-// warp's 32 words, and at D = 2688 a token is 10 full chunks and a half-width tail (88 CTAs).
-// Measured per layer (B200, 23 layers, z = 0.90) against 192 (14 chunks, 24 of 32 lanes busy):
-// B = 1 7.6 vs 7.7 us, B = 3 10.9 vs 14.1 us, B = 8 30.0 vs 33.0 us. HSD_DECODE_CHUNK=128 or
-// 192 forces a narrower form. A token's arithmetic depends on the chunk width only (which
-// words share a CTA), so with one width for all batch sizes a row of any batch (a verify row
-// in particular) equals the same token decoded alone, bit for bit.
-inline int chunk_choice(int) {
-  static int forced = [] {
-    const char* e = getenv("HSD_DECODE_CHUNK");
-    return e ? atoi(e) : 0;
-  }();
-  if (forced == 128 || forced == 192 || forced == 256) return forced;
-  return 256;
+template <typename HT, typename ST, typename YT, int C>
+int dispatch_rg(const DecodeParams& p, cudaStream_t st) {
+  static const int forced = env_int("HSD_DECODE_RG");
+  const int rg = (forced == 8 || forced == 16) ? forced : (p.B == 1 ? 16 : 8);
+  if (rg == 16) return launch_decode<HT, ST, YT, C, 16, 1>(p, st);
+  return launch_decode<HT, ST, YT, C, 8, 2>(p, st);
 }
 
 template <typename HT, typename ST, typename YT>
 int dispatch_c(const DecodeParams& p, cudaStream_t st) {
-  switch (chunk_choice(p.B)) {
-    case 128: return launch_decode<HT, ST, YT, 128>(p, st);
-    case 256: return launch_decode<HT, ST, YT, 256>(p, st);
+  static const int forced = env_int("HSD_DECODE_CHUNK");
+  switch (forced) {
+    case 128: return dispatch_rg<HT, ST, YT, 128>(p, st);
+    case 160: return dispatch_rg<HT, ST, YT, 160>(p, st);
+    case 192: return dispatch_rg<HT, ST, YT, 192>(p, st);
   }
-  return launch_decode<HT, ST, YT, 192>(p, st);
+  return dispatch_rg<HT, ST, YT, 256>(p, st);
 }
 
 template <typename HT, typename ST>

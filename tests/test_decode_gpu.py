@@ -82,8 +82,8 @@ def test_odd_shapes(cuda, dims):
 
 @pytest.mark.gpu
 def test_dense_rows_more_than_one_stage(cuda):
-    """No zeros at all: every row live (1856 rows a CTA), so a CTA stages its rows in more
-    than one sub-batch of its 1024-row ring."""
+    """No zeros at all: every row live (64 rows a group), so every group takes several rounds
+    of register loads."""
     c = synth.decode_case(seed=4, B=1, zero_frac=0.001, device=cuda)
     y = run(c, layouts(c), out_dtype=torch.float32)
     assert rel_err(f32_np(y), oracle_y(c)) < TOL
@@ -216,20 +216,20 @@ torch.save(y.cpu(), sys.argv[2])
 
 
 @pytest.mark.gpu
-def test_ring_shape_does_not_change_bits(cuda, tmp_path):
-    """The staging ring's shape (rows per slot, slots in flight; forced through the
-    HSD_DECODE_SBR / HSD_DECODE_RING variables, read once per process) changes how the
-    copies are scheduled, never the arithmetic: 1x256, 4x64 and 2x512 rows give the same bits
-    on a case with ~900 live rows per CTA (several sub-batches, refilled slots)."""
+def test_launch_shape_does_not_change_bits(cuda, tmp_path):
+    """The live rows loaded per round trip (HSD_DECODE_RG: 16 for one token, 8 for a batch)
+    and the CTAs per SM (shared memory padded through HSD_DECODE_SMEM) change how the work is
+    scheduled, never the arithmetic (the variables are read once per process): the same bits
+    on a case with ~32 live rows per group (every group takes several round trips)."""
     import os
     import subprocess
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     pkg = os.path.join(os.path.dirname(here), "mlx-heimr-sparse-down_b200")
     outs = []
-    for sbr, ring in ((256, 1), (64, 4), (512, 2)):
-        f = tmp_path / f"y_{sbr}_{ring}.pt"
-        env = dict(os.environ, HSD_DECODE_SBR=str(sbr), HSD_DECODE_RING=str(ring))
+    for rg, smem in ((16, 0), (8, 0), (16, 200000)):
+        f = tmp_path / f"y_{rg}_{smem}.pt"
+        env = dict(os.environ, HSD_DECODE_RG=str(rg), HSD_DECODE_SMEM=str(smem))
         subprocess.run([sys.executable, "-c", _RING_SCRIPT, pkg, str(f)], env=env, check=True, timeout=300)
         outs.append(torch.load(f))
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])

@@ -83,12 +83,13 @@ def test_noalloc_matches_workspace_entry_two_calls(cuda):
 
 @pytest.mark.gpu
 def test_noalloc_largest_chunk_that_fits(cuda):
-    """The largest chunk the fixed scratch admits at the reference shapes (its A rows reach the
-    end of the array) equals the workspace entry point; one token more is refused."""
+    """The largest chunk the fixed scratch admits at the reference shapes (its scratch reaches
+    the array's last tenth) equals the workspace entry point; one token more is refused."""
     cap = ctypes.c_size_t(0)
     L.call("hsd_prefill_noalloc_max_bytes", ctypes.byref(cap))
     T = largest_chunk(cap.value, **REF)
-    assert scratch_bytes(T, **REF) > cap.value - (1 << 20)      # the end of the array is in use
+    assert scratch_bytes(T, **REF) > 0.9 * cap.value            # the array's last tenth is in use
+    assert scratch_bytes(T + 1, **REF) > cap.value
     c = synth.decode_case(seed=53, B=T, zero_frac=0.9, routing="zipf", device=cuda)
     lay = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"]) + hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
     tiles = hp.build_tiles(c["sel"], c["E"], hp.GEMM_TT)
