@@ -85,9 +85,10 @@ struct DecodeSmem {
   uint32_t ch[kNGL][2][64];                     // per warp and group: h (raw bits) of the compacted live rows
   short cj[kNGL][2][64];                        //   ... and their rows
   float red[kNGL][C];                           // the group lanes' partial chunks
-  float part[C];                                // this CTA's partial output chunk
   float recv[C];                                // [rank][C/8]: the slices pushed to this CTA
   uint32_t hs[2 * kNGL][64];                    // the round's h values (raw; 64 entries of up to 4 bytes)
+  int64_t grow[2 * kNGL];                       // the round's groups' first neuron rows
+  int64_t gmrow[2 * kNGL];                      //   ... and scale / bias rows
   int gsrc[2 * kNGL];                           // the round's expert ids (-1 shared, -2 none)
   float ggain[2 * kNGL];                        // and gains
   unsigned long long rbar;                      // arrival of the 8 partial slices (st.async)
@@ -368,6 +369,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MI
       }
       S.gsrc[lane] = src;
       S.ggain[lane] = gain;
+      // the group's first neuron row (in rows of its weight array) and its scale / bias row
+      const int loc = (src >= 0) ? g - (g / GF) * GF : g - p.topk * GF;
+      S.grow[lane] = (src >= 0) ? static_cast<int64_t>(src) * p.F + static_cast<int64_t>(loc) * kGS
+                                : static_cast<int64_t>(loc) * kGS;
+      S.gmrow[lane] = (src >= 0) ? static_cast<int64_t>(src) * GF + loc : loc;
     }
     cp_commit_wait();
     __syncthreads();
@@ -381,7 +387,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MI
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int gi = warp + kNGL * i;              // the group's index in this round
-      const int g = r0 + gi;
       const int src = S.gsrc[gi];
       srcs[i] = src;
       const bool valid = src != -2;                 // (g >= g_hi is stored as -2)
@@ -400,10 +405,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MI
       const unsigned me = p.all_rows ? (valid ? 0xffffffffu : 0u) : __ballot_sync(0xffffffffu, valid && RowMath<HT>::live(h0));
       const unsigned mo = p.all_rows ? (valid ? 0xffffffffu : 0u) : __ballot_sync(0xffffffffu, valid && RowMath<HT>::live(h1));
       n[i] = __popc(me) + __popc(mo);
-      const int loc = valid ? ((src >= 0) ? g - (g / GF) * GF : g - p.topk * GF) : 0;
-      const int64_t row0 = (src >= 0) ? static_cast<int64_t>(src) * p.F + static_cast<int64_t>(loc) * kGS
-                                      : static_cast<int64_t>(loc) * kGS;
-      rows[i] = ((src >= 0) ? p.pw : p.spw) + row0 * p.NW + w0;          // word w0 of the group's row 0
+      rows[i] = ((src >= 0) ? p.pw : p.spw) + S.grow[gi] * p.NW + w0;   // word w0 of the group's row 0
       // compaction: row 2l+par goes to entry (live rows below it) = popc(me below l(+1)) + popc(mo below l)
       const unsigned below = (1u << lane) - 1u;     // lanes below this one
       const int eo = __popc(mo & below);
@@ -442,22 +444,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MI
       __syncwarp(0xfu);
       if (i == 0 ? ml0 : ml1) {
         const int src = i == 0 ? srcs[0] : srcs[1];
-        const int g = r0 + warp + kNGL * i;
-        const int loc = (src >= 0) ? g - (g / GF) * GF : g - p.topk * GF;
-        const int64_t mrow = (src >= 0) ? static_cast<int64_t>(src) * GF + loc : loc;
+        const int64_t mrow = S.gmrow[warp + kNGL * i];
         const uint16_t* base = (src >= 0) ? (sb ? p.pb : p.ps) : (sb ? p.spb : p.sps);
         bulk_g2s(&S.meta[warp][i][sb][0], base + mrow * p.D + static_cast<int64_t>(w0) * 8, mbytes, wbar, pol);
       }
     }
     cp_commit_wait();
     __syncwarp();
-    if (wbytes != 0) {                           // warp-uniform
-      if (!mbar_wait_bounded(wbar, wphase)) {
-        if (lane == 0) hsd_flag_decode(HSD_ERR_TIMEOUT);
-        mbar_wait_bounded(wbar, wphase);         // once more for the copies still in flight
-      }
-      wphase ^= 1u;
-    }
+    bool meta_in = wbytes == 0;                  // warp-uniform
     // ---- 3. accumulate and fold, the lane's groups in ascending order
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -472,6 +466,14 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MI
         cp_commit_wait();
         __syncwarp();
         consume_rows<HT, RG, NWC>(&S.stage[warp][i][0][0], t0, n[i], hv0[i], hv1[i], lane, acc, hsum);
+      }
+      if (!meta_in) {                            // the chunks are needed from the first fold on
+        if (!mbar_wait_bounded(wbar, wphase)) {
+          if (lane == 0) hsd_flag_decode(HSD_ERR_TIMEOUT);
+          mbar_wait_bounded(wbar, wphase);       // once more for the copies still in flight
+        }
+        wphase ^= 1u;
+        meta_in = true;
       }
       const float h8 = 8.f * hsum;               // exact
       if (active) {
@@ -496,12 +498,16 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MI
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // before the next round's bulk copies
   }
 
-  // ---- 4. the 16 group lanes, reduced in a fixed order into S.part
+  // ---- 4. the 16 group lanes' partial chunks into shared memory
   if (lane < NWC) {
     *reinterpret_cast<float4*>(&S.red[warp][lane * 8]) = make_float4(out[0], out[1], out[2], out[3]);
     *reinterpret_cast<float4*>(&S.red[warp][lane * 8 + 4]) = make_float4(out[4], out[5], out[6], out[7]);
   }
   __syncthreads();
+  // ---- 5. the cluster's 8 partials: slice r of every CTA's chunk goes to CTA r (st.async,
+  //         completing on CTA r's rbar), which sums the 8 slices in rank order; each output's
+  //         partial is pushed by the thread that sums its 16 group lanes
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // every rbar is initialised
   for (int o = tid; o < C; o += THREADS) {       // 4 partial sums of 4 lanes, then their sum
     float q4[4];
 #pragma unroll
@@ -511,16 +517,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MI
       for (int L = 4 * qd; L < 4 * qd + 4; ++L) a += S.red[L][o];
       q4[qd] = a;
     }
-    S.part[o] = (q4[0] + q4[1]) + (q4[2] + q4[3]);
-  }
-  // ---- 5. the cluster's 8 partials: slice r of every CTA's chunk goes to CTA r (st.async,
-  //         completing on CTA r's rbar), which sums the 8 slices in rank order
-  __syncthreads();
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");   // every rbar is initialised
-  for (int o = tid; o < C; o += THREADS) {
+    const float part = (q4[0] + q4[1]) + (q4[2] + q4[3]);
     const int dst = o / per;
-    st_async_f32(mapa_u32(smem_u32(&S.recv[rank * per + (o - dst * per)]), dst), S.part[o],
-                 mapa_u32(rbar, dst));
+    st_async_f32(mapa_u32(smem_u32(&S.recv[rank * per + (o - dst * per)]), dst), part, mapa_u32(rbar, dst));
   }
   if (!mbar_wait_cluster_bounded(rbar, 0)) {
     if (tid == 0) hsd_flag_decode(HSD_ERR_TIMEOUT);
