@@ -440,21 +440,23 @@ def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512):
 
 
 def ep_leg(layers, device, dist_on, reps=10):
-    """Expert-parallel MoE down projection across the ranks (layer 0's experts sharded E/G per
-    GPU, tokens on their home rank): batch decode B = 64 and a prefill chunk of 512 tokens per
-    rank (weak scaling), NCCL all-to-all dispatch / combine around this library's kernels.
-    Every leg is checked against the single-GPU operator on the same tokens with all 128
-    experts resident (rel_err = max|ep - single| / max|single|, bar 5e-3).
-    -> dict of tokens/s summed over ranks (device time, max over ranks) and the parity."""
-    import torch.distributed as dist
+    """Expert-parallel MoE down projection across the ranks (layer 0's experts sharded round
+    robin, E/G per GPU, tokens on their home rank): batch decode B = 64 and a prefill chunk of
+    512 tokens per rank (weak scaling), NCCL all-to-all dispatch / combine around this library's
+    kernels; at one GPU the same code path with local copies for the exchanges (the baseline of
+    the scaling curve). Every leg is checked against the single-GPU operator on the same tokens
+    with all 128 experts resident (rel_err = max|ep - single| / max|single|, bar 5e-3), and the
+    phases of one call (dispatch, compute, combine) are timed with CUDA events on every rank.
+    -> dict of tokens/s summed over ranks (device time, max over ranks), parity, phases."""
     hsd_b200 = _hsd()
-    from hsd_b200.ep import ExpertParallelDown
-    world, rank = dist.get_world_size(), dist.get_rank()
-    EL = E // world
+    from hsd_b200.ep import ExpertParallelDown, shard_experts
+    if dist_on:
+        import torch.distributed as dist
+        world, rank = dist.get_world_size(), dist.get_rank()
+    else:
+        world, rank = 1, 0
     pw, ps, pb, spw, sps, spb = layers[0]
-    ep = ExpertParallelDown(E, F, FS, D, TOPK, pw[rank * EL:(rank + 1) * EL].contiguous(),
-                            ps[rank * EL:(rank + 1) * EL].contiguous(), pb[rank * EL:(rank + 1) * EL].contiguous(),
-                            spw, sps, spb)
+    ep = ExpertParallelDown(E, F, FS, D, TOPK, *shard_experts(pw, ps, pb, rank, world), spw, sps, spb)
     out, worst = {}, 0.0
     for name, T in (("batch_decode_B64", 64), ("prefill_chunk_512", 512)):
         gen = torch.Generator(device=device).manual_seed(100 + rank)
@@ -462,22 +464,35 @@ def ep_leg(layers, device, dist_on, reps=10):
         gains = torch.cat([sc, torch.ones((T, 1), device=device)], 1).contiguous()
         h = synth.relu2_activations((T, TOPK * F + FS), 0.90, gen, device)
         ms = timed(lambda _: ep(h, sel, gains), reps, 3, device, dist_on) / reps
-        y_ep = ep(h, sel, gains)
-        if T <= 8 * 8:
+        ep.timing = True
+        ph = {}
+        for _ in range(3):                       # the phases of a few calls, last one kept
+            y_ep = ep(h, sel, gains)
+            ph = ep.phase_ms()
+        ep.timing = False
+        if T <= 64:
             y_one = hsd_b200.sparse_down(h, sel, gains, *layers[0], F=F, FS=FS, D=D, topk=TOPK,
                                          out_dtype=torch.float32)
         else:
             y_one = hsd_b200.sparse_down_prefill(h, sel, gains, *layers[0], F=F, FS=FS, D=D, topk=TOPK, E=E,
                                                  out_dtype=torch.float32)
         err = float((y_ep - y_one).abs().max() / y_one.abs().max().clamp_min(1e-30))
-        errs = torch.tensor([err], dtype=torch.float64, device=device)
-        dist.all_reduce(errs, op=dist.ReduceOp.MAX)
-        worst = max(worst, float(errs.item()))
-        out[name] = {"ms": ms, "tokens_per_s_all_ranks": world * T / (ms / 1e3), "rel_err": float(errs.item())}
+        vals = torch.tensor([err, ph["dispatch"], ph["compute"], ph["combine"], ph["total"]], dtype=torch.float64,
+                            device=device)
+        if dist_on:
+            import torch.distributed as dist
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        v = vals.tolist()
+        worst = max(worst, v[0])
+        out[name] = {"ms": ms, "tokens_per_s_all_ranks": world * T / (ms / 1e3),
+                     "tokens_per_s_per_gpu": T / (ms / 1e3), "rel_err": v[0],
+                     "phases_ms_max_over_ranks": {"dispatch": v[1], "compute": v[2], "combine": v[3], "total": v[4]}}
     out["gpus"] = world
     out["parity_ok"] = worst < 5e-3
-    out["note"] = ("experts 0..127 split 128/G per GPU; slots exchanged with NCCL all_to_all_single; rel_err = "
-                   "max over ranks of max|ep - single-GPU operator| / max|single| on the same tokens")
+    out["note"] = ("experts placed round robin (e % G), E/G per GPU; one packed all_to_all_single of the slots' h "
+                   "rows, local ids and gains after an all_to_all of the counts, fp32 partials back; at one GPU the "
+                   "exchanges are local copies; rel_err = max over ranks of max|ep - single-GPU operator| / "
+                   "max|single| on the same tokens; phases: CUDA events of one call, max over ranks")
     return out
 
 
@@ -753,7 +768,7 @@ def main():
     if not args.no_prefill:
         prefill = {"chunk512": prefill_leg(layers, device, dist_on),
                    "chunk2048": prefill_leg(layers, device, dist_on, chunk=2048)}
-    ep = ep_leg(layers, device, dist_on) if dist_on else None
+    ep = ep_leg(layers, device, dist_on)
 
     mamba = None
     if world == 1 and not args.no_mamba:

@@ -36,15 +36,13 @@ def _worker(rank, port, q):
     try:
         import hsd_b200
         from hsd_b200 import synth
-        from hsd_b200.ep import ExpertParallelDown
+        from hsd_b200.ep import ExpertParallelDown, shard_experts
         out = []
         for T in (8, 512):                  # batch decode rows, a prefill chunk, per rank
             c = synth.decode_case(seed=5, B=T * WORLD, zero_frac=0.9, device=dev, routing="zipf")
             pw, ps, pb = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"])
             spw, sps, spb = hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
-            EL = c["E"] // WORLD
-            ep = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"], pw[rank * EL:(rank + 1) * EL].contiguous(),
-                                    ps[rank * EL:(rank + 1) * EL].contiguous(), pb[rank * EL:(rank + 1) * EL].contiguous(),
+            ep = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"], *shard_experts(pw, ps, pb, rank, WORLD),
                                     spw, sps, spb)
             lo, hi = rank * T, (rank + 1) * T
             y = ep(c["h"][lo:hi].contiguous(), c["sel"][lo:hi].contiguous(), c["gains"][lo:hi].contiguous())
@@ -75,3 +73,25 @@ def test_ep_two_gpus_matches_single_gpu(cuda):
     for rank, out in res:
         for T, err in out:
             assert err < 5e-3, (rank, T, err)      # decode-kernel form exact to fp32 order; GEMM form fp16 operands
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [8, 512])
+def test_ep_one_gpu_path_matches_operator(cuda, T):
+    """The expert-parallel code path at world size 1 (no process group: the exchanges are local
+    copies, every expert local) equals the single-GPU operator on the same tokens: the packing,
+    the slot order, the per-slot kernels and the combine, on the hardware of a 1-GPU box."""
+    import hsd_b200
+    from hsd_b200 import synth
+    from hsd_b200.ep import ExpertParallelDown
+    c = synth.decode_case(seed=6, B=T, zero_frac=0.9, device=cuda, routing="zipf")
+    pw, ps, pb = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"])
+    spw, sps, spb = hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
+    ep = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"], pw, ps, pb, spw, sps, spb, timing=True)
+    y = ep(c["h"], c["sel"], c["gains"])
+    ref = hsd_b200.sparse_down(c["h"], c["sel"], c["gains"], pw, ps, pb, spw, sps, spb, F=c["F"], FS=c["FS"],
+                               D=c["D"], topk=c["topk"], out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) < 5e-3
+    ph = ep.phase_ms()
+    assert ph["total"] > 0 and set(ph) == {"dispatch", "compute", "combine", "total"}
