@@ -383,7 +383,7 @@ def cpu_steps(host, ins, steps, warmup=1, budget_s=None):
     return nbytes / dt / 1e9, 1e3 * dt / n, cores, n
 
 
-def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512):
+def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512, dead_groups=0):
     """Config 2: T tokens in chunks of `chunk` through one MoE layer (layer 0), Zipf(1.1)
     routing, h = relu(N(-1.28, 1))^2. Times tile order + gather + tcgen05 GEMM + reduce per
     chunk (CUDA events, max over ranks) -> dict with tensor-pipe and byte rates.
@@ -398,6 +398,12 @@ def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512):
     sel, sc = synth.route_zipf(T, E, TOPK, gen, device)
     gains = torch.cat([sc, torch.ones((T, 1), device=device)], 1).contiguous()
     h = synth.relu2_activations((T, TOPK * F + FS), 0.90, gen, device)
+    if dead_groups:
+        # correlated zeros (a trained model's dead neuron groups): every dead_groups-th 64-group
+        # of every slot is zero for all tokens, K-tiles the GEMM skips
+        cols = torch.arange(TOPK * F + FS, device=device)
+        grp = torch.where(cols < TOPK * F, (cols % F) // 64, (cols - TOPK * F) // 64)
+        h[:, grp % dead_groups == 0] = 0
     lay = layers[0]
     y = torch.empty((T, D), dtype=torch.bfloat16, device=device)
     ws = torch.empty(hp.workspace_bytes(chunk, D, F, FS, TOPK, E), dtype=torch.uint8, device=device)
@@ -424,14 +430,15 @@ def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512):
         if os.path.exists(os.path.join(REPO, "MEASURED_PEAKS.json")) else 1590.0
     wbytes = len(chunks) * (E * F * D // 2 + E * (F // 64) * D * 4 + FS * D // 2 + (FS // 64) * D * 4)
     s = ms / 1e3
-    return {"workload": f"config2: {T} tokens in chunks of {chunk}, one MoE layer, Zipf(1.1) top-6, z=0.90",
+    dead = f", every {dead_groups}th 64-group zero for all tokens (skipped K-tiles)" if dead_groups else ""
+    return {"workload": f"config2: {T} tokens in chunks of {chunk}, one MoE layer, Zipf(1.1) top-6, z=0.90{dead}",
             "ms": ms, "tokens_per_s": T / s,
             "dense_equiv_tflops": dense / s / 1e12,
             "tensor_frac": dense / s / 1e12 / peak_t,
             "useful_tflops": useful / s / 1e12,
             "useful_frac": useful / s / 1e12 / peak_t,
-            "executed_mma_tflops": ex / s / 1e12,
-            "executed_frac": ex / s / 1e12 / peak_t,
+            "executed_mma_tflops": None if dead_groups else ex / s / 1e12,
+            "executed_frac": None if dead_groups else ex / s / 1e12 / peak_t,
             "peak_tflops": peak_t,
             "weight_GBps": wbytes / s / 1e9,
             "note": "tensor_frac = dense-equivalent 2*T*(6F+FS)*D per second over the measured bf16 burst peak; "
@@ -731,7 +738,9 @@ def main():
 
     layers = make_layers(device)
     if args.only_prefill:
-        print(json.dumps({"prefill": prefill_leg(layers, device, dist_on, reps=steps)}), flush=True)
+        print(json.dumps({"prefill": {"chunk512": prefill_leg(layers, device, dist_on, reps=steps),
+                                      "chunk512_every2nd_group_dead": prefill_leg(layers, device, dist_on, reps=steps,
+                                                                                  dead_groups=2)}}), flush=True)
         if dist_on:
             import torch.distributed as dist
             dist.destroy_process_group()
@@ -767,7 +776,8 @@ def main():
     prefill = None
     if not args.no_prefill:
         prefill = {"chunk512": prefill_leg(layers, device, dist_on),
-                   "chunk2048": prefill_leg(layers, device, dist_on, chunk=2048)}
+                   "chunk2048": prefill_leg(layers, device, dist_on, chunk=2048),
+                   "chunk512_every2nd_group_dead": prefill_leg(layers, device, dist_on, dead_groups=2)}
     ep = ep_leg(layers, device, dist_on)
 
     mamba = None

@@ -155,36 +155,47 @@ __global__ void __launch_bounds__(256) build_union_kernel(const HT* __restrict__
 
 // A operand: hc[tile*tt + m, c] = fp16(h[slot's columns][c]), c < the tile's K, zero rows for
 // padding slots; 8 columns (one 16-byte store) per thread. Rows of empty tiles are skipped.
+// One CTA per (64-column group, tile): its 128 A rows' 64 columns as fp16 (8 lanes a row, 16
+// bytes a lane, coalesced both ways), and one byte of the tile's live-K-tile mask,
+// kmask[tile][group] = 1 iff any of them is nonzero (rows of mask_row_bytes(kmax) bytes) --
+// the tensor-core GEMM skips the K-tiles whose byte is 0 (only zeros to multiply). Every byte a
+// non-empty tile's GEMM uses is written here, so the mask needs no clearing.
 template <typename HT>
 __global__ void __launch_bounds__(256) gather_kernel(const HT* __restrict__ h,
                                                      const int32_t* __restrict__ tile_e,
                                                      const int32_t* __restrict__ tile_slot, int tt,
                                                      int F, int FS, int topk, int E, int kmax,
-                                                     __half* __restrict__ hc, int64_t nrows) {
-  const int64_t g = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  const int vpr = kmax / 8;
-  const int64_t row = g / vpr;
-  const int c8 = static_cast<int>(g - row * vpr) * 8;
-  if (row >= nrows) return;
-  const int tile = static_cast<int>(row / tt);
+                                                     __half* __restrict__ hc, uint8_t* __restrict__ kmask) {
+  const int grp = blockIdx.x, tile = blockIdx.y;
   const int e = tile_e[tile];
   if (e < 0) return;
   const bool shared = e >= E;
   const int FF = shared ? FS : F;
-  if (c8 >= FF) return;
-  const int s = tile_slot[row];
+  const int c8 = grp * 64 + (threadIdx.x & 7) * 8;
   const int64_t NR = static_cast<int64_t>(topk) * F + FS;
-  __align__(16) __half v[8];
-  if (s < 0) {
+  bool nz = false;
+  if (grp * 64 < FF) {
+    for (int r = threadIdx.x >> 3; r < tt; r += 32) {
+      const int64_t row = static_cast<int64_t>(tile) * tt + r;
+      const int s = tile_slot[row];
+      __align__(16) __half v[8];
+      if (s < 0) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __float2half_rn(0.f);
-  } else {
-    const int64_t o = (shared ? s * NR + static_cast<int64_t>(topk) * F
-                              : (s / topk) * NR + static_cast<int64_t>(s % topk) * F) + c8;
+        for (int i = 0; i < 8; ++i) v[i] = __float2half_rn(0.f);
+      } else {
+        const int64_t o = (shared ? s * NR + static_cast<int64_t>(topk) * F
+                                  : (s / topk) * NR + static_cast<int64_t>(s % topk) * F) + c8;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __float2half_rn(hsd::to_f32<HT>(h[o + i]));
+        for (int i = 0; i < 8; ++i) {
+          v[i] = __float2half_rn(hsd::to_f32<HT>(h[o + i]));
+          nz |= (__half_as_ushort(v[i]) & 0x7FFFu) != 0u;
+        }
+      }
+      *reinterpret_cast<uint4*>(hc + row * kmax + c8) = *reinterpret_cast<const uint4*>(v);
+    }
   }
-  *reinterpret_cast<uint4*>(hc + row * kmax + c8) = *reinterpret_cast<const uint4*>(v);
+  const int live = __syncthreads_or(nz);
+  if (threadIdx.x == 0 && kmask) kmask[static_cast<int64_t>(tile) * hsd::mask_row_bytes(kmax) + grp] = live ? 1 : 0;
 }
 
 // y[t, o] = sum_{p = 0..topk} part[t*(topk+1) + p, o] (+ resid), fixed order.
@@ -219,22 +230,20 @@ int prefill_tile_counts(int T, int topk, int E, int tt, int* nt_routed, int* nt_
 }
 
 int launch_gather(const void* h, int h_dtype, const int32_t* tile_e, const int32_t* tile_slot, int NT,
-                  int tt, int F, int FS, int topk, int E, int kmax, __half* hc, cudaStream_t st) {
-  const int64_t nrows = static_cast<int64_t>(NT) * tt;
-  const int64_t n = nrows * (kmax / 8);
-  const unsigned grid = static_cast<unsigned>((n + 255) / 256);
+                  int tt, int F, int FS, int topk, int E, int kmax, __half* hc, uint8_t* kmask, cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>(kmax / 64), static_cast<unsigned>(NT));
   switch (h_dtype) {
     case HSD_F32:
       gather_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(h), tile_e, tile_slot, tt, F, FS,
-                                                 topk, E, kmax, hc, nrows);
+                                                 topk, E, kmax, hc, kmask);
       break;
     case HSD_F16:
       gather_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(h), tile_e, tile_slot, tt, F, FS,
-                                                  topk, E, kmax, hc, nrows);
+                                                  topk, E, kmax, hc, kmask);
       break;
     case HSD_BF16:
       gather_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(h), tile_e,
-                                                         tile_slot, tt, F, FS, topk, E, kmax, hc, nrows);
+                                                         tile_slot, tt, F, FS, topk, E, kmax, hc, kmask);
       break;
     default: return set_error(HSD_ERR_DTYPE, "prefill gather: h_dtype %d", h_dtype);
   }
@@ -304,16 +313,17 @@ extern "C" int hsd_prefill_build_union(const void* h, int h_dtype, const int32_t
 
 namespace {
 struct PrefillWorkspace {
-  size_t hc_off, hc_bytes, part_off, part_bytes, total;
+  size_t km_off, hc_off, hc_bytes, part_off, part_bytes, total;
 };
 int prefill_workspace(int T, int D, int F, int FS, int topk, int E, PrefillWorkspace* w) {
   int nr = 0, ns = 0;
   int rc = hsd::prefill_tile_counts(T, topk, E, hsd::kPrefillTile, &nr, &ns);
   if (rc) return rc;
   const size_t kmax = static_cast<size_t>(F > FS ? F : FS);
-  w->hc_off = 0;
+  w->km_off = 0;
+  w->hc_off = (static_cast<size_t>(nr + ns) * hsd::mask_row_bytes(static_cast<int>(kmax)) + 255) / 256 * 256;
   w->hc_bytes = static_cast<size_t>(nr + ns) * hsd::kPrefillTile * kmax * 2;
-  w->part_off = (w->hc_bytes + 255) / 256 * 256;
+  w->part_off = (w->hc_off + w->hc_bytes + 255) / 256 * 256;
   w->part_bytes = static_cast<size_t>(T) * (topk + 1) * D * 4;
   w->total = w->part_off + w->part_bytes;
   return HSD_OK;
@@ -359,13 +369,14 @@ extern "C" int hsd_sparse_down_prefill(const void* h, int h_dtype, const float* 
       return hsd::set_error(HSD_ERR_ALIGN, "hsd_sparse_down_prefill: weights and workspace must be 16-byte aligned");
   cudaStream_t st = hsd::as_stream(stream);
   unsigned char* ws = static_cast<unsigned char*>(workspace);
+  uint8_t* kmask = ws + w.km_off;
   __half* hc = reinterpret_cast<__half*>(ws + w.hc_off);
   float* part = reinterpret_cast<float*>(ws + w.part_off);
   const int kmax = F > FS ? F : FS;
-  rc = hsd::launch_gather(h, h_dtype, tile_e, tile_slot, NT, hsd::kPrefillTile, F, FS, topk, E, kmax, hc, st);
+  rc = hsd::launch_gather(h, h_dtype, tile_e, tile_slot, NT, hsd::kPrefillTile, F, FS, topk, E, kmax, hc, kmask, st);
   if (rc) return rc;
-  rc = hsd::launch_prefill_gemm(hc, kmax, tile_e, tile_slot, NT, gains, pw, ps, pb, s_dtype, spw, sps, spb, part, T, D,
-                                F, FS, topk, E, st);
+  rc = hsd::launch_prefill_gemm(hc, kmax, tile_e, tile_slot, NT, kmask, gains, pw, ps, pb, s_dtype, spw, sps, spb,
+                                part, T, D, F, FS, topk, E, st);
   if (rc) return rc;
   return hsd::launch_reduce(part, resid, y, y_dtype, T, D, topk, topk + (FS > 0 ? 1 : 0), st);
 }

@@ -10,17 +10,23 @@ namespace hsd {
 // Tiles of the fixed tile order for (T, topk, E, tt): routed, then shared.
 int prefill_tile_counts(int T, int topk, int E, int tt, int* nt_routed, int* nt_shared);
 
-// hc[tile*tt + m, c] = fp16(h[slot's columns][c]) for the rows of non-empty tiles.
+// Bytes of one tile's live-K-tile mask: one per 64-column group, rounded up to 8.
+__host__ __device__ inline int mask_row_bytes(int kmax) { return (kmax / 64 + 7) / 8 * 8; }
+
+// hc[tile*tt + m, c] = fp16(h[slot's columns][c]) for the rows of non-empty tiles, and
+// kmask[tile][mask_row_bytes(kmax)]: 1 iff the tile has a nonzero A value in columns
+// [64g, 64g + 64).
 int launch_gather(const void* h, int h_dtype, const int32_t* tile_e, const int32_t* tile_slot, int NT,
-                  int tt, int F, int FS, int topk, int E, int kmax, __half* hc, cudaStream_t st);
+                  int tt, int F, int FS, int topk, int E, int kmax, __half* hc, uint8_t* kmask, cudaStream_t st);
 
 // y[t] = sum over the token's first nparts partial rows (+ resid), fixed order.
 int launch_reduce(const float* part, const void* resid, void* y, int y_dtype, int T, int D, int topk,
                   int nparts, cudaStream_t st);
 
 // The tensor-core grouped GEMM over the tile order (hsd_prefill_gemm.cu).
+// kmask: the gather's live-K-tile bytes; K-tiles whose byte is 0 are skipped.
 int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const int32_t* tile_slot, int NT,
-                        const float* gains, const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
+                        const uint8_t* kmask, const float* gains, const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
                         const uint32_t* spw, const void* sps, const void* spb, float* part, int T, int D,
                         int F, int FS, int topk, int E, cudaStream_t st);
 

@@ -89,8 +89,20 @@ struct GemmParams {
   const uint16_t* sps;
   const uint16_t* spb;
   float* part;
-  int NT, T, D, F, FS, topk, E, nnt;
+  const uint8_t* kmask;    // [NT][KG] live-K-tile bytes from the gather (KG: kmax / 64 rounded up to 8)
+  int NT, T, D, F, FS, topk, E, nnt, KG;
 };
+
+// Whether a role processes K-tile kt of a tile: when the tile has a nonzero A value in it, or
+// when it is the tile's last K-tile and none was processed before (an all-zero tile still
+// writes its accumulator: zeros). `done` counts the K-tiles processed so far; `word` caches
+// the 8 mask bytes of kt's 8-aligned block (rows of KG bytes, KG a multiple of 8). Every role
+// applies the same rule to the same bytes, so all roles walk the same K-tiles.
+__device__ __forceinline__ bool kt_run(const GemmParams& p, int tile, int kt, int KT, int done, uint64_t& word) {
+  if ((kt & 7) == 0)
+    word = __ldg(reinterpret_cast<const unsigned long long*>(p.kmask + static_cast<int64_t>(tile) * p.KG + kt));
+  return ((word >> (8 * (kt & 7))) & 0xFFu) != 0 || (kt == KT - 1 && done == 0);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -247,7 +259,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (e < 0) continue;
         const bool shared = e >= p.E;
         const int KT = shared ? GFS : GF;              // 0 for shared tiles when FS == 0: skipped
+        int done = 0;
+        uint64_t mword = 0;
         for (int kt = 0; kt < KT; ++kt) {
+          if (!kt_run(p, tile, kt, KT, done, mword)) continue;   // only zeros to multiply
+          ++done;
           if (!mbar_wait(bar_empty(stage), ph ^ 1u)) {
             ok = false;
             break;
@@ -283,7 +299,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(bar_acc_empty(acc), aph ^ 1u)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc) * ACC_COLS;
+        uint32_t accum = 0;                                // the item's first MMA overwrites
+        int done = 0;
+        uint64_t mword = 0;
         for (int kt = 0; kt < KT; ++kt) {
+          if (!kt_run(p, tile, kt, KT, done, mword)) continue;
+          ++done;
           if (!mbar_wait(bar_full_tma(stage), ph) || !mbar_wait(bar_bfull(bj), bph)) {
             ok = false;
             break;
@@ -291,9 +312,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
           const uint32_t a0 = base + OFF_A + stage * A_BYTES, b0 = base + OFF_B + bj * B_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_f16(d, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 2048, B_LBO, 1024),
-                     (kt | kk) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            umma_f16(d, sw128_desc(a0 + kk * 32, 16, 1024), sw128_desc(b0 + kk * 2048, B_LBO, 1024), accum);
+            accum = 1u;
+          }
           umma_commit(bar_empty(stage));                   // frees the A / W stage when these MMAs finish
           umma_commit(bar_bempty(bj));                     // and the B buffer
           if (++stage == STAGES) {
@@ -370,7 +392,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int e = p.tile_e[tile];
       if (e < 0) continue;
       const int KT = (e >= p.E) ? GFS : GF;
+      int done = 0;
+      uint64_t mword = 0;
       for (int kt = 0; kt < KT; ++kt) {
+        if (!kt_run(p, tile, kt, KT, done, mword)) continue;
+        ++done;
         // (the stage's previous fp16 pairs were read before its previous MMAs, which came
         // before the producer refilled it: the full barrier alone orders the overwrite)
         if (!mbar_wait(bar_full_tma(stage), ph)) {
@@ -413,7 +439,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int e = p.tile_e[tile];
       if (e < 0) continue;
       const int KT = (e >= p.E) ? GFS : GF;
+      int done = 0;
+      uint64_t mword = 0;
       for (int kt = 0; kt < KT; ++kt) {
+        if (!kt_run(p, tile, kt, KT, done, mword)) continue;
+        ++done;
         if (!mbar_wait(bar_full_tma(stage), ph) || !mbar_wait(bar_conv(stage), ph) ||
             !mbar_wait(bar_bempty(bj), bph ^ 1u)) {
           ok = false;
@@ -515,7 +545,7 @@ int launch_typed(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap
 namespace hsd {
 
 int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const int32_t* tile_slot, int NT,
-                        const float* gains, const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
+                        const uint8_t* kmask, const float* gains, const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
                         const uint32_t* spw, const void* sps, const void* spb, float* part, int T, int D,
                         int F, int FS, int topk, int E, cudaStream_t st) {
   if (D % BN != 0 || F % BK != 0 || FS < 0 || FS % BK != 0 || kmax % BK != 0)
@@ -545,6 +575,8 @@ int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const
   p.sps = static_cast<const uint16_t*>(sps);
   p.spb = static_cast<const uint16_t*>(spb);
   p.part = part;
+  p.kmask = kmask;
+  p.KG = (kmax / BK + 7) / 8 * 8;
   p.NT = NT;
   p.T = T;
   p.D = D;

@@ -2,8 +2,8 @@
 // cudaMalloc: code running while a CUDA graph is being captured without a memory pool,
 // runtimes that own every device allocation themselves, or hosts that must not grow device
 // memory after start-up. It computes exactly what hsd_sparse_down_prefill computes, but
-// keeps its scratch (the compacted tile order, the gathered fp16 A rows and the fp32
-// partial rows) in one file-scope device array of kNoAllocScratchBytes instead of a
+// keeps its scratch (the compacted tile order, the live-K-tile masks, the gathered fp16 A
+// rows and the fp32 partial rows) in one file-scope device array of kNoAllocScratchBytes instead of a
 // caller workspace. Every GPU that loads this library holds that array until the process
 // exits. Calls share the array, so calls whose work overlaps on the GPU (two streams, or
 // two host threads) race; calls ordered on one stream do not.
@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(1024) compact_tiles_kernel(const int32_t* __re
 
 struct NoAllocLayout {
   int NC;                 // capacity of the compacted tile order
-  size_t te_off, ts_off, hc_off, part_off, total;
+  size_t te_off, ts_off, km_off, hc_off, part_off, total;
 };
 
 // Non-empty tiles are at most: every full tile of slots plus one partial tile per expert
@@ -85,7 +85,8 @@ int noalloc_layout(int T, int D, int F, int FS, int topk, int E, int NT, NoAlloc
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
   L->te_off = 0;
   L->ts_off = up(L->te_off + sizeof(int32_t) * L->NC);
-  L->hc_off = up(L->ts_off + sizeof(int32_t) * static_cast<size_t>(L->NC) * hsd::kPrefillTile);
+  L->km_off = up(L->ts_off + sizeof(int32_t) * static_cast<size_t>(L->NC) * hsd::kPrefillTile);
+  L->hc_off = up(L->km_off + static_cast<size_t>(L->NC) * hsd::mask_row_bytes(static_cast<int>(kmax)));
   L->part_off = up(L->hc_off + static_cast<size_t>(L->NC) * hsd::kPrefillTile * kmax * 2);
   L->total = L->part_off + static_cast<size_t>(T) * (topk + 1) * D * 4;
   if (NT != nr + ns)
@@ -142,19 +143,20 @@ extern "C" int hsd_sparse_down_prefill_noalloc(const void* h, int h_dtype, const
   unsigned char* ws = static_cast<unsigned char*>(base);
   int32_t* te_c = reinterpret_cast<int32_t*>(ws + L.te_off);
   int32_t* ts_c = reinterpret_cast<int32_t*>(ws + L.ts_off);
+  uint8_t* kmask = ws + L.km_off;
   __half* hc = reinterpret_cast<__half*>(ws + L.hc_off);
   float* part = reinterpret_cast<float*>(ws + L.part_off);
   cudaStream_t st = hsd::as_stream(stream);
   // every scratch byte the later kernels read is written first in this call: the compacted
-  // tile order in full, the A rows of every non-empty tile (zero rows for padding slots),
-  // and every partial row of every token; nothing has to start at zero
+  // tile order in full, the live-K-tile mask bytes and the A rows of every non-empty tile
+  // (zero rows for padding slots), and every partial row of every token
   compact_tiles_kernel<<<1, 1024, 0, st>>>(tile_e, tile_slot, NT, hsd::kPrefillTile, L.NC, te_c, ts_c);
   rc = hsd::check_launch("hsd_sparse_down_prefill_noalloc: compact");
   if (rc) return rc;
   const int kmax = F > FS ? F : FS;
-  rc = hsd::launch_gather(h, h_dtype, te_c, ts_c, L.NC, hsd::kPrefillTile, F, FS, topk, E, kmax, hc, st);
+  rc = hsd::launch_gather(h, h_dtype, te_c, ts_c, L.NC, hsd::kPrefillTile, F, FS, topk, E, kmax, hc, kmask, st);
   if (rc) return rc;
-  rc = hsd::launch_prefill_gemm(hc, kmax, te_c, ts_c, L.NC, gains, pw, ps, pb, s_dtype, spw, sps, spb, part, T, D, F,
+  rc = hsd::launch_prefill_gemm(hc, kmax, te_c, ts_c, L.NC, kmask, gains, pw, ps, pb, s_dtype, spw, sps, spb, part, T, D, F,
                                 FS, topk, E, st);
   if (rc) return rc;
   return hsd::launch_reduce(part, resid, y, y_dtype, T, D, topk, topk + (FS > 0 ? 1 : 0), st);

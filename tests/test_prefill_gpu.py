@@ -100,3 +100,33 @@ def test_prefill_resid_dtype_and_given_tiles(cuda):
     assert rel_err(f32_np(y), f32_np(resid.float() + y32)) < 1e-2   # bf16 rounding of resid + y
     # deterministic: the same bits twice
     assert torch.equal(y32, hp.sparse_down_prefill(c["h"], c["sel"], c["gains"], *lay, out_dtype=torch.float32, **kw))
+
+
+@pytest.mark.gpu
+def test_prefill_skips_dead_k_tiles_exactly(cuda):
+    """Correlated zeros (a trained model's dead neuron groups): every third 64-group of every
+    slot is zero for all tokens, and one rarely chosen expert's slots are zero throughout, so
+    its tiles have no live K-tile at all. The GEMM skips those K-tiles (the gather's masks);
+    the result still matches the oracle, the decode kernel, and the same call with the dead
+    groups holding an exact zero everywhere -- the skipped work only ever added zeros."""
+    T = 512
+    c = synth.decode_case(seed=61, B=T, zero_frac=0.9, device=cuda, routing="zipf")
+    F, FS, topk = c["F"], c["FS"], c["topk"]
+    h = c["h"].clone()
+    cols = torch.arange(topk * F + FS, device=cuda)
+    grp = torch.where(cols < topk * F, (cols % F) // 64, (cols - topk * F) // 64)
+    h[:, grp % 3 == 0] = 0
+    rare = int(torch.bincount(c["sel"].reshape(-1).long(), minlength=c["E"]).argmin())
+    for k in range(topk):
+        h[c["sel"][:, k] == rare, k * F:(k + 1) * F] = 0
+    lay = layouts(c)
+    kw = dict(F=F, FS=FS, D=c["D"], topk=topk)
+    y = hp.sparse_down_prefill(h, c["sel"], c["gains"], *lay, E=c["E"], out_dtype=torch.float32, **kw)
+    c2 = dict(c, h=h)
+    rows = np.random.default_rng(1).choice(T, 64, replace=False)
+    assert rel_err(f32_np(y)[rows], oracle_rows(c2, rows)) < TOL
+    yd = hsd_b200.sparse_down(h, c["sel"], c["gains"], *lay, out_dtype=torch.float32, **kw)
+    assert rel_err(f32_np(y), f32_np(yd)) < TOL
+    assert torch.equal(y, hp.sparse_down_prefill(h, c["sel"], c["gains"], *lay, E=c["E"], out_dtype=torch.float32,
+                                                 **kw))
+    assert hsd_b200.device_status() == 0

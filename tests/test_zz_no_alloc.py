@@ -24,12 +24,13 @@ REF = dict(D=2688, F=1856, FS=3712, topk=6, E=128)   # the reference model's MoE
 def scratch_bytes(T, D, F, FS, topk, E, tt=hp.GEMM_TT):
     """The scratch a call needs, as the library lays it out: the compacted tile order (at most
     every full tile of slots + one partial tile per expert with slots + the shared expert's
-    tiles), the fp16 A rows of those tiles and the fp32 partial rows."""
+    tiles), their live-K-tile masks, the fp16 A rows of those tiles and the fp32 partial rows."""
     nr, ns = hp.num_tiles(T, topk, E, tt)
     slots = T * topk
     nc = min(nr, slots // tt + min(E, slots)) + ns
     up = lambda x: (x + 255) // 256 * 256  # noqa: E731
-    hc_off = up(up(4 * nc) + 4 * nc * tt)
+    mask_row = (max(F, FS) // 64 + 7) // 8 * 8                 # a mask byte per K-tile, rows of 8
+    hc_off = up(up(up(4 * nc) + 4 * nc * tt) + nc * mask_row)
     part_off = up(hc_off + nc * tt * max(F, FS) * 2)
     return part_off + T * (topk + 1) * D * 4
 
