@@ -511,7 +511,8 @@ def mamba_leg(device, reps=50, n_layers=23, ks=(2, 3)):
     Reports us per layer for the whole block, for the scan kernel alone (with GB/s on its
     state traffic: the 2 MiB state read + 1+k per-row 2 MiB checkpoints written), and for the
     rollback: one device int on the resident buffers, or the copying form
-    (hsd_mamba_rollback: 2 MiB state + conv window) with its GB/s."""
+    (hsd_mamba_rollback: 2 MiB state + conv window in one kernel, the n_layers copies replayed
+    from a CUDA graph) with its GB/s on read + write bytes."""
     _hsd()
     from hsd_b200 import mamba as hm
     blocks = [hm.random_mamba2(300 + l, device=device) for l in range(n_layers)]
@@ -570,11 +571,19 @@ def mamba_leg(device, reps=50, n_layers=23, ks=(2, 3)):
         conv_out = torch.empty((b0.K - 1, b0.conv_dim), dtype=torch.bfloat16, device=device)
         state_out = torch.empty((b0.H, b0.P, b0.N), dtype=torch.float32, device=device)
 
-        def rb(i):
+        def rb_body():
             for rc in rcs:
-                hm.rollback_into(rc.padded, rc.states, 1 + (i % L), conv_out, state_out)
+                hm.rollback_into(rc.padded, rc.states, L, conv_out, state_out)
 
-        ms_rb = timed(rb, reps, 3, device, False, label="hsd_mamba") / reps
+        st2 = torch.cuda.Stream(device)
+        st2.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(st2):
+            rb_body()
+        torch.cuda.current_stream(device).wait_stream(st2)
+        g_rb = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_rb):
+            rb_body()
+        ms_rb = timed(lambda _: g_rb.replay(), reps, 3, device, False, label="hsd_mamba") / reps
         scan_bytes = state_b * (1 + L) + L * (b0.conv_dim + b0.H) * 2 + L * b0.I * 4
         rb_bytes = 2 * state_b + 2 * (b0.K - 1) * b0.conv_dim * 2
         res[f"k{k}"] = {"rows": L,

@@ -24,6 +24,8 @@
 // over the same buffers. Each thread (conv) or lane (ssm) reads its whole slice before it
 // writes any of it, and only its own slice, so the in-place update needs no barrier. A
 // rollback is then one integer written on the device.
+#include <algorithm>
+
 #include "hsd_common.cuh"
 
 HSD_DEFINE_STATUS(mamba)
@@ -44,6 +46,21 @@ __device__ __forceinline__ int read_keep(const int* n_keep, int rows) {
 template <typename T>
 __device__ __forceinline__ float ld(const void* p, int64_t i) {
   return hsd::to_f32<T>(reinterpret_cast<const T*>(p)[i]);
+}
+
+// Four consecutive values at element index i (4-element aligned) as fp32, one vector load.
+template <typename T>
+__device__ __forceinline__ void ld4(const void* p, int64_t i, float* out) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i));
+    out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+  } else {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const T*>(p) + i));
+    out[0] = hsd::bits16_to_f32<T>(static_cast<uint16_t>(v.x & 0xffffu));
+    out[1] = hsd::bits16_to_f32<T>(static_cast<uint16_t>(v.x >> 16));
+    out[2] = hsd::bits16_to_f32<T>(static_cast<uint16_t>(v.y & 0xffffu));
+    out[3] = hsd::bits16_to_f32<T>(static_cast<uint16_t>(v.y >> 16));
+  }
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
@@ -102,39 +119,93 @@ __global__ void __launch_bounds__(256) ssm_verify_kernel(const void* xbc, int64_
   const int64_t sbase = (static_cast<int64_t>(h) * P + p) * N + lane * NPL;   // this lane's slice
   if (n_keep) state0 = states + static_cast<int64_t>(read_keep(n_keep, rows) - 1) * H * P * N;
   float st[NPL];
+  if constexpr (NPL % 4 == 0) {
 #pragma unroll
-  for (int i = 0; i < NPL; ++i) st[i] = state0 ? state0[sbase + i] : 0.f;
+    for (int i = 0; i < NPL; i += 4) {
+      const float4 v = state0 ? *reinterpret_cast<const float4*>(state0 + sbase + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      st[i] = v.x; st[i + 1] = v.y; st[i + 2] = v.z; st[i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) st[i] = state0 ? state0[sbase + i] : 0.f;
+  }
   const float A = -expf(A_log[h]);
   const float dbias = dt_bias[h], Dh = Dp[h];
-  for (int t = 0; t < L; ++t) {
-    const int64_t row = static_cast<int64_t>(t) * xbc_stride;
-    const float x = ld<TX>(xbc, row + static_cast<int64_t>(h) * P + p);
-    const float dtt = fminf(fmaxf(softplus_f(ld<TD>(dt, static_cast<int64_t>(t) * dt_stride + h) + dbias), dt_min), dt_max);
-    const float dA = expf(dtt * A);
-    const float dx = dtt * x;
-    const int64_t bo = row + I + static_cast<int64_t>(g) * N + lane * NPL;
-    const int64_t co = row + I + static_cast<int64_t>(G) * N + static_cast<int64_t>(g) * N + lane * NPL;
-    float acc = 0.f;
+  // Rows in batches of RB: a batch's inputs (x, dt, B and C slices) do not depend on the state,
+  // so all of them are loaded before the first row is computed -- one memory round trip per
+  // batch instead of one per row; the rows are then run one after another as single steps.
+  constexpr int RB = 4;
+  for (int t0 = 0; t0 < L; t0 += RB) {
+    float xr[RB], dtr[RB], br[RB][NPL], cr[RB][NPL];
 #pragma unroll
-    for (int i = 0; i < NPL; ++i) {
-      st[i] = fmaf(st[i], dA, dx * ld<TX>(xbc, bo + i));
-      acc = fmaf(st[i], ld<TX>(xbc, co + i), acc);
+    for (int r = 0; r < RB; ++r) {
+      const int t = t0 + r;
+      if (t < L) {
+        const int64_t row = static_cast<int64_t>(t) * xbc_stride;
+        xr[r] = ld<TX>(xbc, row + static_cast<int64_t>(h) * P + p);
+        dtr[r] = ld<TD>(dt, static_cast<int64_t>(t) * dt_stride + h);
+        const int64_t bo = row + I + static_cast<int64_t>(g) * N + lane * NPL;
+        const int64_t co = row + I + static_cast<int64_t>(G) * N + static_cast<int64_t>(g) * N + lane * NPL;
+        if constexpr (NPL % 4 == 0) {             // 4 consecutive values per vector load (the host
+#pragma unroll                                       // checked 4-element alignment of xbc rows)
+          for (int i = 0; i < NPL; i += 4) {
+            ld4<TX>(xbc, bo + i, &br[r][i]);
+            ld4<TX>(xbc, co + i, &cr[r][i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < NPL; ++i) {
+            br[r][i] = ld<TX>(xbc, bo + i);
+            cr[r][i] = ld<TX>(xbc, co + i);
+          }
+        }
+      }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0)
-      reinterpret_cast<TY*>(y)[static_cast<int64_t>(t) * I + static_cast<int64_t>(h) * P + p] =
-          hsd::from_f32<TY>(fmaf(Dh, x, acc));
-    if (last_only && t != L - 1) continue;         // prefill: the final state only, in states[0]
-    float* dst = states + static_cast<int64_t>(last_only ? 0 : t) * H * P * N + sbase;
-    if constexpr (NPL % 4 == 0) {
+    for (int r = 0; r < RB; ++r) {
+      const int t = t0 + r;
+      if (t >= L) break;
+      const float x = xr[r];
+      const float dtt = fminf(fmaxf(softplus_f(dtr[r] + dbias), dt_min), dt_max);
+      const float dA = expf(dtt * A);
+      const float dx = dtt * x;
+      float acc = 0.f;
 #pragma unroll
-      for (int i = 0; i < NPL; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(st[i], st[i + 1], st[i + 2], st[i + 3]);
-    } else {
+      for (int i = 0; i < NPL; ++i) {
+        st[i] = fmaf(st[i], dA, dx * br[r][i]);
+        acc = fmaf(st[i], cr[r][i], acc);
+      }
 #pragma unroll
-      for (int i = 0; i < NPL; ++i) dst[i] = st[i];
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0)
+        reinterpret_cast<TY*>(y)[static_cast<int64_t>(t) * I + static_cast<int64_t>(h) * P + p] =
+            hsd::from_f32<TY>(fmaf(Dh, x, acc));
+      if (last_only && t != L - 1) continue;       // prefill: the final state only, in states[0]
+      float* dst = states + static_cast<int64_t>(last_only ? 0 : t) * H * P * N + sbase;
+      if constexpr (NPL % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < NPL; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(st[i], st[i + 1], st[i + 2], st[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) dst[i] = st[i];
+      }
     }
   }
+}
+
+// The copying rollback: the kept row's state (float4 pieces) and the conv window (bytes) in one
+// grid-stride launch.
+__global__ void __launch_bounds__(256) rollback_copy_kernel(const float4* __restrict__ src_state,
+                                                            float4* __restrict__ dst_state, int64_t n4,
+                                                            const unsigned char* __restrict__ src_win,
+                                                            unsigned char* __restrict__ dst_win, int64_t nwin) {
+  hsd::pdl_launch_dependents();
+  hsd::pdl_wait();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride)
+    dst_state[i] = src_state[i];
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nwin; i += stride)
+    dst_win[i] = src_win[i];
 }
 
 template <typename TI, typename TW>
@@ -224,6 +295,9 @@ int ssm_impl(const char* who, const void* xbc, int x_dtype, int64_t xbc_stride, 
     return hsd::set_error(HSD_ERR_SHAPE, "%s: bad shape (H %% G == 0, xbc_stride >= H*P + 2*G*N)", who);
   if (!hsd::aligned(states, 16) || (state0 && !hsd::aligned(state0, 16)))
     return hsd::set_error(HSD_ERR_ALIGN, "%s: states must be 16-byte aligned", who);
+  const int xb = x_dtype == HSD_F32 ? 4 : 2;
+  if (N >= 128 && (!hsd::aligned(xbc, 4 * xb) || (xbc_stride * xb) % (4 * xb) != 0 || (static_cast<int64_t>(H) * P) % 4 != 0))
+    return hsd::set_error(HSD_ERR_ALIGN, "%s: xbc rows must start on 4-element boundaries (N >= 128 uses vector loads)", who);
   const int64_t warps = static_cast<int64_t>(H) * P;
   dim3 grid(static_cast<unsigned>((warps * 32 + 255) / 256));
   cudaStream_t st = hsd::as_stream(stream);
@@ -276,12 +350,16 @@ extern "C" int hsd_mamba_rollback(const float* states, const void* padded, int e
   if (n_keep < 1 || n_keep > L || elem_bytes < 1 || K < 1)
     return hsd::set_error(HSD_ERR_ARG, "hsd_mamba_rollback: need 1 <= n_keep <= L (got n_keep=%d L=%d)", n_keep, L);
   cudaStream_t st = hsd::as_stream(stream);
-  const size_t sbytes = static_cast<size_t>(H) * P * N * sizeof(float);
-  cudaError_t e = cudaMemcpyAsync(state_out, states + static_cast<size_t>(n_keep - 1) * H * P * N, sbytes,
-                                  cudaMemcpyDeviceToDevice, st);
-  if (e != cudaSuccess) return hsd::check_cuda(e, "hsd_mamba_rollback: state copy");
-  const size_t cbytes = static_cast<size_t>(K - 1) * C * elem_bytes;
-  e = cudaMemcpyAsync(conv_out, static_cast<const char*>(padded) + static_cast<size_t>(n_keep) * C * elem_bytes, cbytes,
-                      cudaMemcpyDeviceToDevice, st);
-  return hsd::check_cuda(e, "hsd_mamba_rollback: conv window copy");
+  const int64_t snum = static_cast<int64_t>(H) * P * N;
+  if (snum % 4 != 0 || !hsd::aligned(states, 16) || !hsd::aligned(state_out, 16))
+    return hsd::set_error(HSD_ERR_ALIGN, "hsd_mamba_rollback: states / state_out must be 16-byte aligned, H*P*N %% 4 == 0");
+  const int64_t nwin = static_cast<int64_t>(K - 1) * C * elem_bytes;
+  const int64_t n4 = snum / 4;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n4 + 255) / 256, 148 * 8));
+  cudaError_t e = hsd::launch_pdl(rollback_copy_kernel, dim3(grid), dim3(256), 0, st,
+                                  reinterpret_cast<const float4*>(states + static_cast<int64_t>(n_keep - 1) * snum),
+                                  reinterpret_cast<float4*>(state_out), n4,
+                                  static_cast<const unsigned char*>(padded) + static_cast<int64_t>(n_keep) * C * elem_bytes,
+                                  static_cast<unsigned char*>(conv_out), nwin);
+  return hsd::check_cuda(e, "hsd_mamba_rollback");
 }
