@@ -688,6 +688,7 @@ def main():
     ap.add_argument("--only-prefill", action="store_true", help="profiling: the prefill leg alone")
     ap.add_argument("--no-model", action="store_true", help="skip the config-4 model leg")
     ap.add_argument("--no-mamba", action="store_true", help="skip the config-3 Mamba verify / rollback leg")
+    ap.add_argument("--no-ep", action="store_true", help="skip the expert-parallel leg (profiling runs)")
     ap.add_argument("--model-tokens", type=int, default=256)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--layers", type=int, default=23, help="fewer layers: small profiling case only")
@@ -787,7 +788,7 @@ def main():
         prefill = {"chunk512": prefill_leg(layers, device, dist_on),
                    "chunk2048": prefill_leg(layers, device, dist_on, chunk=2048),
                    "chunk512_every2nd_group_dead": prefill_leg(layers, device, dist_on, dead_groups=2)}
-    ep = ep_leg(layers, device, dist_on)
+    ep = None if args.no_ep else ep_leg(layers, device, dist_on)
 
     mamba = None
     if world == 1 and not args.no_mamba:

@@ -142,8 +142,9 @@ int hsd_prefill_build_union(const void* h, int h_dtype, const int32_t* tile_e,
                             const int32_t* tile_slot, int NT, int tt, int F, int FS, int topk,
                             int E, int umax, int32_t* ulist, int32_t* ucount, void* stream);
 
-/* Workspace bytes hsd_sparse_down_prefill needs for (T, D, F, FS, topk, E): the gathered
- * fp16 A rows of every tile and the fp32 partial rows [T*(topk+1), D]. Host-only. */
+/* Workspace bytes hsd_sparse_down_prefill needs for (T, D, F, FS, topk, E): one live byte per
+ * (tile, 64-neuron group), the gathered fp16 A rows of every tile and the fp32 partial rows
+ * [T*(topk+1), D]. Host-only. */
 int hsd_prefill_workspace_bytes(int T, int D, int F, int FS, int topk, int E, size_t* bytes);
 
 /* hsd/prefill.py:294 sparse_down_prefill(h, sel, gains, pw, ps, pb, spw, sps, spb, *, F, FS,
@@ -151,7 +152,9 @@ int hsd_prefill_workspace_bytes(int T, int D, int F, int FS, int topk, int E, si
  *   h [T, topk*F+FS], gains [T, topk+1] f32, tiles from hsd_prefill_build_tiles with
  *   tt = 128, layouts as for decode -> y [T, D] (+ resid). Gathers the tiles' h rows (fp16),
  *   runs the tcgen05 grouped GEMM (weights dequantised to fp16 in shared memory, fp32
- *   accumulation in TMEM, routing gain in the epilogue) and sums each token's topk+1
+ *   accumulation in TMEM, routing gain in the epilogue; a K-tile -- 64 neurons -- with no
+ *   nonzero h in any of the tile's slots is skipped, hsd/prefill.py:11-16's union at group
+ *   granularity) and sums each token's topk+1
  *   partial rows in a fixed order. The caller provides `workspace` (16-byte aligned) of at
  *   least hsd_prefill_workspace_bytes(). Supported: D % 192 == 0, F % 64 == 0, FS % 64 == 0. */
 int hsd_sparse_down_prefill(const void* h, int h_dtype, const float* gains, const int32_t* tile_e,
@@ -188,7 +191,8 @@ int hsd_mamba_ssm_verify(const void* xbc, int x_dtype, int64_t xbc_stride, const
 
 /* hsd/mamba.py:47 mamba_rollback(records, n_keep), on device and without recomputation:
  * state_out = states[n_keep-1], conv_out = padded[n_keep : n_keep+K-1] (elem_bytes per
- * element). 1 <= n_keep <= L. */
+ * element), one copy kernel. 1 <= n_keep <= L; states and state_out 16-byte aligned and
+ * H*P*N % 4 == 0 (HSD_ERR_ALIGN otherwise). */
 int hsd_mamba_rollback(const float* states, const void* padded, int elem_bytes, int n_keep, int L,
                        int H, int P, int N, int C, int K, float* state_out, void* conv_out,
                        void* stream);
