@@ -449,57 +449,93 @@ def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512, dead_groups
 def ep_leg(layers, device, dist_on, reps=10):
     """Expert-parallel MoE down projection across the ranks (layer 0's experts sharded round
     robin, E/G per GPU, tokens on their home rank): batch decode B = 64 and a prefill chunk of
-    512 tokens per rank (weak scaling), NCCL all-to-all dispatch / combine around this library's
-    kernels; at one GPU the same code path with local copies for the exchanges (the baseline of
-    the scaling curve). Every leg is checked against the single-GPU operator on the same tokens
+    512 tokens per rank (weak scaling). Two forms: the product (ExpertParallelDown: dispatch and
+    combine through peer memory by this library's kernels, the GEMM's epilogue storing partial
+    rows into their home rank; timed eagerly and replayed from a CUDA graph) and the baseline
+    (ExpertParallelDownCollective: NCCL all_to_all around the same kernels, one host read of the
+    counts per call). At one GPU both run the same code path on local memory (the base of the
+    scaling curve). Every form is checked against the single-GPU operator on the same tokens
     with all 128 experts resident (rel_err = max|ep - single| / max|single|, bar 5e-3), and the
-    phases of one call (dispatch, compute, combine) are timed with CUDA events on every rank.
-    -> dict of tokens/s summed over ranks (device time, max over ranks), parity, phases."""
+    phases of one call are timed with CUDA events on every rank.
+    -> dict of tokens/s (device time, max over ranks), parity, phases."""
     hsd_b200 = _hsd()
-    from hsd_b200.ep import ExpertParallelDown, shard_experts
+    from hsd_b200.ep import ExpertParallelDown, ExpertParallelDownCollective, shard_experts
     if dist_on:
         import torch.distributed as dist
         world, rank = dist.get_world_size(), dist.get_rank()
     else:
         world, rank = 1, 0
     pw, ps, pb, spw, sps, spb = layers[0]
-    ep = ExpertParallelDown(E, F, FS, D, TOPK, *shard_experts(pw, ps, pb, rank, world), spw, sps, spb)
+    mine = shard_experts(pw, ps, pb, rank, world)
+    p2p = ExpertParallelDown(E, F, FS, D, TOPK, *mine, spw, sps, spb, max_tokens=512)
+    coll = ExpertParallelDownCollective(E, F, FS, D, TOPK, *mine, spw, sps, spb)
+
+    def phases(ep, h, sel, gains):
+        ep.timing = True
+        ph = {}
+        for _ in range(3):                       # the phases of a few calls, the last one kept
+            y = ep(h, sel, gains)
+            ph = ep.phase_ms()
+        ep.timing = False
+        return y, ph
+
+    def max_ranks(vals):
+        t = torch.tensor(vals, dtype=torch.float64, device=device)
+        if dist_on:
+            import torch.distributed as dist
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
     out, worst = {}, 0.0
     for name, T in (("batch_decode_B64", 64), ("prefill_chunk_512", 512)):
         gen = torch.Generator(device=device).manual_seed(100 + rank)
         sel, sc = synth.route_zipf(T, E, TOPK, gen, device)
         gains = torch.cat([sc, torch.ones((T, 1), device=device)], 1).contiguous()
         h = synth.relu2_activations((T, TOPK * F + FS), 0.90, gen, device)
-        ms = timed(lambda _: ep(h, sel, gains), reps, 3, device, dist_on) / reps
-        ep.timing = True
-        ph = {}
-        for _ in range(3):                       # the phases of a few calls, last one kept
-            y_ep = ep(h, sel, gains)
-            ph = ep.phase_ms()
-        ep.timing = False
         if T <= 64:
             y_one = hsd_b200.sparse_down(h, sel, gains, *layers[0], F=F, FS=FS, D=D, topk=TOPK,
                                          out_dtype=torch.float32)
         else:
             y_one = hsd_b200.sparse_down_prefill(h, sel, gains, *layers[0], F=F, FS=FS, D=D, topk=TOPK, E=E,
                                                  out_dtype=torch.float32)
-        err = float((y_ep - y_one).abs().max() / y_one.abs().max().clamp_min(1e-30))
-        vals = torch.tensor([err, ph["dispatch"], ph["compute"], ph["combine"], ph["total"]], dtype=torch.float64,
-                            device=device)
-        if dist_on:
-            import torch.distributed as dist
-            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-        v = vals.tolist()
-        worst = max(worst, v[0])
-        out[name] = {"ms": ms, "tokens_per_s_all_ranks": world * T / (ms / 1e3),
-                     "tokens_per_s_per_gpu": T / (ms / 1e3), "rel_err": v[0],
-                     "phases_ms_max_over_ranks": {"dispatch": v[1], "compute": v[2], "combine": v[3], "total": v[4]}}
+        den = y_one.abs().max().clamp_min(1e-30)
+        ms_p2p = timed(lambda _: p2p(h, sel, gains), reps, 3, device, dist_on) / reps
+        y_p2p, ph_p2p = phases(p2p, h, sel, gains)
+        # the same call replayed from a CUDA graph (nothing in it waits on the host)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                y_graph = p2p(h, sel, gains)
+        torch.cuda.current_stream(device).wait_stream(side)
+        ms_graph = timed(lambda _: graph.replay(), reps, 3, device, dist_on) / reps
+        torch.cuda.synchronize(device)
+        err_graph = float((y_graph - y_one).abs().max() / den)
+        del graph
+        ms_coll = timed(lambda _: coll(h, sel, gains), reps, 3, device, dist_on) / reps
+        y_coll, ph_coll = phases(coll, h, sel, gains)
+        errs = [float((y_p2p - y_one).abs().max() / den), err_graph, float((y_coll - y_one).abs().max() / den)]
+        keys_p, keys_c = ("dispatch", "shared", "expert", "combine", "total"), ("dispatch", "compute", "combine", "total")
+        v = max_ranks(errs + [ph_p2p[k] for k in keys_p] + [ph_coll[k] for k in keys_c])
+        worst = max(worst, *v[:3])
+        out[name] = {"ms": ms_graph, "tokens_per_s_all_ranks": world * T / (ms_graph / 1e3),
+                     "tokens_per_s_per_gpu": T / (ms_graph / 1e3),
+                     "eager_ms": ms_p2p, "eager_tokens_per_s_per_gpu": T / (ms_p2p / 1e3),
+                     "rel_err": max(v[0], v[1]),
+                     "phases_ms_max_over_ranks": dict(zip(keys_p, v[3:8])),
+                     "collective_baseline": {"ms": ms_coll, "tokens_per_s_per_gpu": T / (ms_coll / 1e3),
+                                             "rel_err": v[2], "phases_ms_max_over_ranks": dict(zip(keys_c, v[8:12]))}}
+    p2p.inboxes.close()
     out["gpus"] = world
     out["parity_ok"] = worst < 5e-3
-    out["note"] = ("experts placed round robin (e % G), E/G per GPU; one packed all_to_all_single of the slots' h "
-                   "rows, local ids and gains after an all_to_all of the counts, fp32 partials back; at one GPU the "
-                   "exchanges are local copies; rel_err = max over ranks of max|ep - single-GPU operator| / "
-                   "max|single| on the same tokens; phases: CUDA events of one call, max over ranks")
+    out["note"] = ("experts placed round robin (e % G), E/G per GPU. ms / tokens_per_s: the peer-memory form "
+                   "(hsd_ep_dispatch / hsd_ep_expert / hsd_ep_combine: plain stores into the other GPUs' inboxes "
+                   "over NVLink, release / acquire flags, no host read) replayed from a CUDA graph; eager_*: the "
+                   "same calls launched from Python; collective_baseline: NCCL all_to_all_single exchanges around "
+                   "the same kernels with one host read of the counts per call. rel_err = max over ranks and forms "
+                   "of max|ep - single-GPU operator| / max|single| on the same tokens; phases: CUDA events of one "
+                   "eager call, max over ranks")
     return out
 
 

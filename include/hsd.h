@@ -328,6 +328,59 @@ int hsd_sparse_down_prefill_noalloc(const void* h, int h_dtype, const float* gai
                                     const void* spb, const void* resid, void* y, int y_dtype,
                                     int T, int D, int F, int FS, int topk, int E, void* stream);
 
+/* ---- expert parallelism over the GPUs of one box ----------------------------------- */
+
+/* The MoE down projection with the routed experts sharded round robin over `world` GPUs
+ * (expert e on rank e % world, local index e / world), the shared expert replicated and
+ * every token on its home rank: a multi-GPU form of hsd/decode.py:164 sparse_down and
+ * hsd/prefill.py:294 sparse_down_prefill (the reference has one GPU). One process per GPU.
+ * The exchange is this library's own: every rank's INBOX (hsd_ep_alloc memory, mapped into
+ * the other ranks' processes with the IPC calls below) is written by the others with plain
+ * stores over NVLink, ordered by release/acquire flags at system scope; no collective
+ * library, no multicast, nothing read back to the host (a call can be captured in a CUDA
+ * graph). A call is hsd_ep_dispatch, then hsd_ep_expert, then hsd_ep_combine, on one stream;
+ * every rank makes the same calls in the same order with the same (world, max_tokens, topk,
+ * F, D, E); B may differ between ranks and may be 0. One inbox and workspace serve every
+ * call and every layer of a rank. Every device-side wait for another rank is bounded by
+ * timeout_s (<= 0: 10 s); running out records HSD_ERR_TIMEOUT in the status word, the call's
+ * output is unspecified and the ranks must allocate their buffers again. */
+#define HSD_EP_IPC_HANDLE_BYTES 64
+
+/* Bytes of a rank's inbox and of its private workspace (256-byte aligned, from any
+ * allocator). At world 8, max_tokens 512 and the reference shapes: 124 MB and 100 MB. */
+int hsd_ep_buffer_bytes(int world, int max_tokens, int topk, int F, int D, int E,
+                        size_t* inbox_bytes, size_t* workspace_bytes);
+/* Zeroed device memory that other processes can map (cudaMalloc; free with hsd_ep_free).
+ * The one allocation this library makes, and only here. */
+int hsd_ep_alloc(size_t bytes, void** ptr);
+int hsd_ep_free(void* ptr);
+/* The HSD_EP_IPC_HANDLE_BYTES-byte handle of hsd_ep_alloc memory, its mapping in another
+ * process (with peer access enabled), and the unmapping. */
+int hsd_ep_ipc_handle(const void* ptr, void* handle);
+int hsd_ep_ipc_open(const void* handle, void** ptr);
+int hsd_ep_ipc_close(void* ptr);
+/* Stores the inboxes of ranks 0..world-1 as this process addresses them (its own included)
+ * in the workspace; once, before the first call. Synchronises the stream. */
+int hsd_ep_set_peers(void* workspace, const uint64_t* inbox_addrs, int world, void* stream);
+/* Routes this rank's B tokens: hcat [B, topk*F + FS] (bf16 or f16, 16-byte aligned), sel
+ * [B, topk] int32 global expert ids, gains [B, topk+1] f32. Each (token, slot) row goes to its
+ * expert's owner with its local id and gain. An id outside [0, E) is recorded as
+ * HSD_ERR_INDEX and the slot contributes nothing defined. */
+int hsd_ep_dispatch(void* workspace, int rank, int world, int max_tokens, const void* hcat,
+                    int h_dtype, const int32_t* sel, const float* gains, int B, int topk, int F,
+                    int FS, int D, int E, double timeout_s, void* stream);
+/* The owner's side: the slots this rank received times its experts pw [E/world, F, D/8],
+ * ps / pb [E/world, F/64, D] (neuron-major, s_dtype bf16 or f16, owned_experts order) with
+ * the tensor-core GEMM, each fp32 partial row times its gain stored into its home rank's
+ * inbox. inbox: this rank's own inbox. */
+int hsd_ep_expert(void* workspace, void* inbox, int rank, int world, int max_tokens,
+                  const uint32_t* pw, const void* ps, const void* pb, int s_dtype, int h_dtype,
+                  int topk, int F, int D, int E, double timeout_s, void* stream);
+/* y [B, D] f32 = the sum over each token's topk partial rows in slot order, + y_shared [B, D]
+ * f32 when given (the shared expert of the same tokens, computed by the caller). */
+int hsd_ep_combine(void* workspace, int rank, int world, int max_tokens, const float* y_shared,
+                   float* y, int B, int topk, int F, int D, int E, double timeout_s, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

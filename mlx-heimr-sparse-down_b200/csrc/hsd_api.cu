@@ -28,6 +28,7 @@ int hsd_read_status_mamba(int* out, cudaStream_t st);
 int hsd_read_status_norm(int* out, cudaStream_t st);
 int hsd_read_status_attn(int* out, cudaStream_t st);
 int hsd_read_status_qmma(int* out, cudaStream_t st);
+int hsd_read_status_ep(int* out, cudaStream_t st);
 
 extern "C" const char* hsd_last_error_string(void) { return hsd::g_last_error; }
 
@@ -40,7 +41,8 @@ extern "C" int hsd_device_status(int* status_out, void* stream) {
   int (*readers[])(int*, cudaStream_t) = {hsd_read_status_decode, hsd_read_status_prefill,
                                                 hsd_read_status_gemm, hsd_read_status_up,
                                                 hsd_read_status_mamba, hsd_read_status_norm,
-                                                hsd_read_status_attn, hsd_read_status_qmma};
+                                                hsd_read_status_attn, hsd_read_status_qmma,
+                                                hsd_read_status_ep};
   for (auto rd : readers) {
     int v = HSD_OK;
     int rc = rd(&v, st);

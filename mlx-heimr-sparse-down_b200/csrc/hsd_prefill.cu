@@ -27,6 +27,7 @@ constexpr int kMaxExperts = 256;
 __global__ void __launch_bounds__(kTileThreads) build_tiles_kernel(const int32_t* __restrict__ sel,
                                                                    int T, int topk, int E, int tt,
                                                                    int nt_routed, int nt_shared,
+                                                                   const int* __restrict__ nslots_dev,
                                                                    int32_t* __restrict__ tile_e,
                                                                    int32_t* __restrict__ tile_slot) {
   __shared__ int cnt[kMaxExperts];
@@ -35,7 +36,7 @@ __global__ void __launch_bounds__(kTileThreads) build_tiles_kernel(const int32_t
   __shared__ int before[kMaxExperts];           // running[] at the start of the chunk
   __shared__ uint16_t tab[kTileWarps][kMaxExperts];   // per chunk: slots of expert e in warp w
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nslots = T * topk;
+  const int nslots = nslots_dev ? min(max(*nslots_dev, 0), T * topk) : T * topk;
   const int NT = nt_routed + nt_shared;
   for (int i = tid; i < E; i += kTileThreads) {
     cnt[i] = 0;
@@ -229,6 +230,15 @@ int prefill_tile_counts(int T, int topk, int E, int tt, int* nt_routed, int* nt_
   return HSD_OK;
 }
 
+int launch_build_tiles(const int32_t* sel, int T, int topk, int E, int tt, int nt_routed, int nt_shared,
+                       const int* nslots_dev, int32_t* tile_e, int32_t* tile_slot, cudaStream_t st) {
+  if (E > kMaxExperts) return set_error(HSD_ERR_SHAPE, "prefill build_tiles: E > %d", kMaxExperts);
+  if (static_cast<long long>(T) * topk > (1ll << 30)) return set_error(HSD_ERR_SHAPE, "prefill build_tiles: too many slots");
+  build_tiles_kernel<<<1, kTileThreads, 0, st>>>(sel, T, topk, E, tt, nt_routed, nt_shared, nslots_dev, tile_e,
+                                                 tile_slot);
+  return check_launch("prefill build_tiles");
+}
+
 int launch_gather(const void* h, int h_dtype, const int32_t* tile_e, const int32_t* tile_slot, int NT,
                   int tt, int F, int FS, int topk, int E, int kmax, __half* hc, uint8_t* kmask, cudaStream_t st) {
   const dim3 grid(static_cast<unsigned>(kmax / 64), static_cast<unsigned>(NT));
@@ -275,14 +285,10 @@ extern "C" int hsd_prefill_num_tiles(int T, int topk, int E, int tt, int* nt_rou
 extern "C" int hsd_prefill_build_tiles(const int32_t* sel, int T, int topk, int E, int tt, int32_t* tile_e,
                                        int32_t* tile_slot, void* stream) {
   if (!sel || !tile_e || !tile_slot) return hsd::set_error(HSD_ERR_ARG, "hsd_prefill_build_tiles: null pointer");
-  if (E > kMaxExperts) return hsd::set_error(HSD_ERR_SHAPE, "hsd_prefill_build_tiles: E > %d", kMaxExperts);
   int nr = 0, ns = 0;
   int rc = hsd::prefill_tile_counts(T, topk, E, tt, &nr, &ns);
   if (rc) return rc;
-  if (static_cast<long long>(T) * topk > (1ll << 30))
-    return hsd::set_error(HSD_ERR_SHAPE, "hsd_prefill_build_tiles: too many slots");
-  build_tiles_kernel<<<1, kTileThreads, 0, hsd::as_stream(stream)>>>(sel, T, topk, E, tt, nr, ns, tile_e, tile_slot);
-  return hsd::check_launch("hsd_prefill_build_tiles");
+  return hsd::launch_build_tiles(sel, T, topk, E, tt, nr, ns, nullptr, tile_e, tile_slot, hsd::as_stream(stream));
 }
 
 extern "C" int hsd_prefill_build_union(const void* h, int h_dtype, const int32_t* tile_e, const int32_t* tile_slot,

@@ -24,11 +24,17 @@ int launch_reduce(const float* part, const void* resid, void* y, int y_dtype, in
                   int nparts, cudaStream_t st);
 
 // The tensor-core grouped GEMM over the tile order (hsd_prefill_gemm.cu).
-// kmask: the gather's live-K-tile bytes; K-tiles whose byte is 0 are skipped.
+// kmask: the gather's live-K-tile bytes; K-tiles whose byte is 0 are skipped. row_dst
+// (optional): slot s's fp32 output row goes to row_dst[s] instead of part's row.
 int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const int32_t* tile_slot, int NT,
                         const uint8_t* kmask, const float* gains, const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
                         const uint32_t* spw, const void* sps, const void* spb, float* part, int T, int D,
-                        int F, int FS, int topk, int E, cudaStream_t st);
+                        int F, int FS, int topk, int E, cudaStream_t st, float* const* row_dst = nullptr);
+
+// The fixed tile order of build_tiles_kernel; with nslots_dev, only the first *nslots_dev
+// slots (read on the device) are placed and the rest count as absent.
+int launch_build_tiles(const int32_t* sel, int T, int topk, int E, int tt, int nt_routed, int nt_shared,
+                       const int* nslots_dev, int32_t* tile_e, int32_t* tile_slot, cudaStream_t st);
 
 constexpr int kPrefillTile = 128;   // slots per tile of the GEMM (its M)
 

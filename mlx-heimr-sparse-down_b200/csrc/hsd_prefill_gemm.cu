@@ -13,8 +13,9 @@
 //                             accumulated in TMEM (two 256-column buffers: the epilogue of one
 //                             item overlaps the MMAs of the next)
 // Epilogue (4 warps, one TMEM lane quadrant each): tcgen05.ld 32 columns at a time, times the
-// slot's routing gain, stored to part[token*(topk+1) + k, :] (fp32). A separate fixed-order
-// reduce sums the topk+1 partial rows of each token.
+// slot's routing gain, stored to part[token*(topk+1) + k, :] (fp32), or -- expert parallelism --
+// to the slot's row of its home GPU's partial buffer through a per-slot pointer table (plain
+// stores over NVLink). A separate fixed-order reduce sums the topk+1 partial rows of each token.
 //
 // Warp roles (19 warps): 0 TMA producer, 1 MMA issuer (and TMEM owner), 2-5 epilogue, 6 scale
 // converter (bf16 -> fp16 pairs), 7-18 dequantisation. A / packed-W stages ring through 7 buffers, dequantised B through 2, each
@@ -89,6 +90,7 @@ struct GemmParams {
   const uint16_t* sps;
   const uint16_t* spb;
   float* part;
+  float* const* row_dst;   // optional: slot s's output row is row_dst[s] (another GPU's memory allowed), not part
   const uint8_t* kmask;    // [NT][KG] live-K-tile bytes from the gather (KG: kmax / 64 rounded up to 8)
   int NT, T, D, F, FS, topk, E, nnt, KG;
 };
@@ -355,18 +357,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int s = p.tile_slot[static_cast<int64_t>(tile) * BM + m];
       int64_t row = -1;
       float g = 0.f;
+      float* out_row = nullptr;
       if (s >= 0) {
         row = (e >= p.E) ? static_cast<int64_t>(s) * (p.topk + 1) + p.topk
                          : static_cast<int64_t>(s / p.topk) * (p.topk + 1) + (s % p.topk);
         g = __ldg(p.gains + row);
+        out_row = p.row_dst ? p.row_dst[s] : p.part + row * p.D;
       }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc) * ACC_COLS;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_ld32(taddr + c0, v);
-        if (row >= 0) {
-          float* dst = p.part + row * p.D + static_cast<int64_t>(nt) * BN + c0;
+        if (out_row) {
+          float* dst = out_row + static_cast<int64_t>(nt) * BN + c0;
 #pragma unroll
           for (int i = 0; i < 32; i += 4)
             *reinterpret_cast<float4*>(dst + i) = make_float4(v[i] * g, v[i + 1] * g, v[i + 2] * g, v[i + 3] * g);
@@ -547,7 +551,7 @@ namespace hsd {
 int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const int32_t* tile_slot, int NT,
                         const uint8_t* kmask, const float* gains, const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
                         const uint32_t* spw, const void* sps, const void* spb, float* part, int T, int D,
-                        int F, int FS, int topk, int E, cudaStream_t st) {
+                        int F, int FS, int topk, int E, cudaStream_t st, float* const* row_dst) {
   if (D % BN != 0 || F % BK != 0 || FS < 0 || FS % BK != 0 || kmax % BK != 0)
     return set_error(HSD_ERR_SHAPE, "prefill gemm: need D %% %d == 0, F and FS %% 64 == 0 (D=%d F=%d FS=%d)", BN,
                      D, F, FS);
@@ -575,6 +579,7 @@ int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const
   p.sps = static_cast<const uint16_t*>(sps);
   p.spb = static_cast<const uint16_t*>(spb);
   p.part = part;
+  p.row_dst = row_dst;
   p.kmask = kmask;
   p.KG = (kmax / BK + 7) / 8 * 8;
   p.NT = NT;

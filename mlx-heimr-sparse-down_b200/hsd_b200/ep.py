@@ -6,33 +6,38 @@ Placement: routed expert e lives on rank e % G (local index e // G), round robin
 popular low-numbered experts of a skewed router spread over every rank (under the Zipf(1.1)
 routing of the benchmark the busiest rank gets ~1.7x the mean slot count, against ~4.9x for
 contiguous blocks of E/G experts at G = 8). The shared expert is replicated. Tokens stay on
-their home rank. One MoE down projection is:
+their home rank.
 
-  dispatch  every (token, slot) goes to its expert's owner as one packed byte row -- its h
-            row (F values), its expert id local to the owner and its routing gain -- in ONE
-            all_to_all_single over NCCL, after an all_to_all of the per-rank slot counts
-  compute   the owner runs this library's kernels on the slots it received, one slot per row
-            (the tcgen05 prefill GEMM, or the decode kernel's routed-only form for a handful of
-            slots), the gain applied in the kernel, fp32 out
-  combine   the fp32 partial rows go back with a second all_to_all_single; the home rank sums
-            each token's topk partials in slot order and adds its own shared-expert part (the
-            decode kernel's shared-only form, or the GEMM with the shared expert as the one
-            routed expert for many tokens). The partials stay fp32: six bf16-rounded
-            partials per token would cost ~2^-9 relative each, most of the parity budget.
+ExpertParallelDown (the product) runs one call as three library calls on the caller's stream,
+exchanging through peer memory: every rank's inbox (PeerInboxes) is mapped into every other
+rank's process and written with plain stores over NVLink, ordered by release / acquire flags
+(include/hsd.h, hsd_ep_*):
 
-The only host synchronisation is the read of the received slot counts (all_to_all_single
-takes its split sizes on the host). Batch-1 latency stays on one GPU (no exchange); this path
-is for batch decode and prefill chunks. With no process group (a single GPU) the exchanges
-are local copies, so the same code path gives the one-GPU baseline.
+  dispatch  each (token, slot)'s h row, local expert id and gain go straight into its owner's
+            inbox (the counts travel the same way first, so nothing is read back to the host)
+  expert    the owner runs the tcgen05 grouped GEMM over the rows it received; the epilogue
+            stores each fp32 partial row, times its gain, into its home rank's inbox
+  combine   the home rank sums each token's topk partials in slot order plus its own
+            shared-expert rows (computed between dispatch and expert, while the rows travel)
+
+The partials stay fp32: six bf16-rounded partials per token would cost ~2^-9 relative each,
+most of the parity budget. With one GPU the same path runs with the rank's own inbox.
+
+ExpertParallelDownCollective is the same computation with torch.distributed all_to_all
+exchanges (NCCL on GPUs, gloo on CPU): the baseline the bench measures beside the product, and
+the form the CPU tests drive with the oracle's arithmetic in place of the kernels.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from .decode import sparse_down
 from .prefill import sparse_down_prefill
 
 GEMM_MIN_SLOTS = 64         # owners with at least this many slots use the tensor-core GEMM
-GEMM_MIN_ROWS = 256         # the shared expert of at least this many tokens uses the GEMM
+GEMM_MIN_ROWS = 32          # the shared expert of at least this many tokens uses the GEMM (measured crossover ~28)
 
 
 def owned_experts(E, rank, world):
@@ -83,8 +88,9 @@ def _kernel_shared_down(spw, sps, spb, FS, D):
     return run
 
 
-class ExpertParallelDown:
-    """The MoE down projection with routed experts sharded round robin over `group`.
+class ExpertParallelDownCollective:
+    """The MoE down projection with routed experts sharded round robin over `group`, exchanged
+    with torch.distributed all_to_all (the baseline of ExpertParallelDown).
 
     pw / ps / pb: this rank's experts (owned_experts order) [E/G, F, D/8] / [E/G, F/64, D]
     (neuron-major; shard_experts slices a full stack); spw / sps / spb: the shared expert
@@ -176,4 +182,162 @@ class ExpertParallelDown:
         if self.FS > 0 and B > 0:
             y = y + self.shared_down(hcat[:, K * F:].contiguous(), gains[:, K:])
         self._mark(3)
+        return y
+
+
+class PeerInboxes:
+    """One rank's expert-parallel buffers: its inbox (hsd_ep_alloc memory that every other rank
+    maps and writes) and its private workspace, with the inboxes of all ranks as this process
+    addresses them stored in the workspace. Construction is collective over `group` (an
+    all_gather of the 64-byte IPC handles and of the configuration, which must agree). One
+    PeerInboxes serves every call and every layer of the rank. close() is collective too: it
+    synchronises the device, waits for every rank, unmaps the peers' inboxes and frees this
+    rank's; without it the memory stays until the process exits."""
+
+    def __init__(self, world, rank, max_tokens, topk, F, D, E, device, group=None):
+        self.world, self.rank, self.max_tokens = world, rank, max_tokens
+        self.topk, self.F, self.D, self.E = topk, F, D, E
+        self.device = torch.device(device)
+        self.group = group
+        ib, wb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+        L.call("hsd_ep_buffer_bytes", world, max_tokens, topk, F, D, E, ctypes.byref(ib), ctypes.byref(wb))
+        self.inbox_bytes, self.workspace_bytes = ib.value, wb.value
+        with torch.cuda.device(self.device):
+            p = ctypes.c_void_p(0)
+            L.call("hsd_ep_alloc", ib.value, ctypes.byref(p))
+            self.inbox = p.value
+            self.workspace = torch.empty(wb.value, dtype=torch.uint8, device=self.device)
+            self._opened = []
+            addrs = [0] * world
+            addrs[rank] = self.inbox
+            if world > 1:
+                handle = (ctypes.c_ubyte * 64)()
+                L.call("hsd_ep_ipc_handle", ctypes.c_void_p(self.inbox), ctypes.cast(handle, ctypes.c_void_p))
+                mine = (bytes(handle), (world, max_tokens, topk, F, D, E))
+                everyone = [None] * world
+                dist.all_gather_object(everyone, mine, group=group)
+                for r, (h, cfg) in enumerate(everyone):
+                    if cfg != mine[1]:
+                        raise ValueError(f"PeerInboxes: rank {r} has configuration {cfg}, this rank {mine[1]}")
+                    if r == rank:
+                        continue
+                    q = ctypes.c_void_p(0)
+                    L.call("hsd_ep_ipc_open", ctypes.cast((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.c_void_p),
+                           ctypes.byref(q))
+                    self._opened.append(q.value)
+                    addrs[r] = q.value
+            table = (ctypes.c_uint64 * world)(*addrs)
+            L.call("hsd_ep_set_peers", L.ptr(self.workspace), ctypes.cast(table, ctypes.c_void_p), world,
+                   L.stream_of(self.workspace))
+
+    def close(self):
+        if self.inbox is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for q in self._opened:
+            L.call("hsd_ep_ipc_close", ctypes.c_void_p(q))
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)            # nobody maps this inbox any more
+        L.call("hsd_ep_free", ctypes.c_void_p(self.inbox))
+        self.inbox = None
+
+
+class ExpertParallelDown:
+    """The MoE down projection with routed experts sharded round robin over `group`, exchanged
+    through peer memory with this library's kernels (no host synchronisation per call: a call
+    can be captured in a CUDA graph).
+
+    pw / ps / pb: this rank's experts (owned_experts order) [E/G, F, D/8] / [E/G, F/64, D]
+    (neuron-major; shard_experts slices a full stack); spw / sps / spb: the shared expert
+    (replicated). max_tokens bounds B per call (it sizes the inbox); inboxes: a PeerInboxes to
+    share between layers (else one is made, collectively). Without an initialised process group
+    the object runs alone (world size 1) on its own inbox. timing=True records CUDA events
+    around the phases of every call; phase_ms() reads the last call's. Every rank must make
+    the same calls in the same order (B may differ, and may be 0)."""
+
+    def __init__(self, E, F, FS, D, topk, pw, ps, pb, spw=None, sps=None, spb=None, group=None, max_tokens=512,
+                 inboxes=None, timeout_s=10.0, timing=False):
+        self.group = group
+        self.distributed = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if self.distributed else 1
+        self.rank = dist.get_rank(group) if self.distributed else 0
+        if E % self.world:
+            raise ValueError(f"ExpertParallelDown: E={E} is not divisible by {self.world} ranks")
+        self.E, self.F, self.FS, self.D, self.topk = E, F, FS, D, topk
+        self.E_local = E // self.world
+        L.require_cuda(pw, ps, pb, spw, sps, spb, what="ExpertParallelDown")
+        if pw.shape[0] != self.E_local:
+            raise ValueError(f"ExpertParallelDown: {pw.shape[0]} local experts given, {self.E_local} expected")
+        self.pw, self.ps, self.pb = pw, ps, pb
+        self.s_code = L.dtype_code(ps, "ExpertParallelDown scales")
+        self.max_tokens = max_tokens
+        self.inboxes = inboxes or PeerInboxes(self.world, self.rank, max_tokens, topk, F, D, E, pw.device, group)
+        ib = self.inboxes
+        if (ib.world, ib.rank, ib.max_tokens, ib.topk, ib.F, ib.D, ib.E) != (self.world, self.rank, max_tokens, topk,
+                                                                         F, D, E):
+            raise ValueError("ExpertParallelDown: the inboxes were made for another configuration")
+        self.shared_down = _kernel_shared_down(spw, sps, spb, FS, D) if FS > 0 else None
+        self.timeout_s = float(timeout_s)
+        self.timing = timing
+        self._events = None
+
+    def owner(self, e):
+        return e % self.world
+
+    def _mark(self, i):
+        if self._events is not None:
+            self._events[i].record()
+
+    def phase_ms(self):
+        """The last timed call's device time per phase (ms) on this rank: dispatch (routing and
+        the rows out), shared (this rank's shared expert), expert (waiting for the rows in, the
+        GEMM and the partial rows out), combine (waiting for the partials in and the sums)."""
+        if self._events is None:
+            return None
+        self._events[-1].synchronize()
+        e = self._events
+        return {"dispatch": e[0].elapsed_time(e[1]), "shared": e[1].elapsed_time(e[2]),
+                "expert": e[2].elapsed_time(e[3]), "combine": e[3].elapsed_time(e[4]),
+                "total": e[0].elapsed_time(e[4])}
+
+    def __call__(self, hcat, sel, gains):
+        """hcat [B, topk*F + FS] bf16 / f16, sel [B, topk] int32 (global ids), gains [B, topk+1]
+        f32 -> y [B, D] f32 for this rank's B tokens (B may be 0; every rank must call)."""
+        B, K, F, D = hcat.shape[0], self.topk, self.F, self.D
+        what = "ExpertParallelDown"
+        L.require_cuda(hcat, sel, gains, what=what)
+        if B > self.max_tokens:
+            raise ValueError(f"{what}: {B} tokens, more than max_tokens={self.max_tokens}")
+        if tuple(hcat.shape) != (B, K * F + self.FS) or tuple(sel.shape) != (B, K) or tuple(gains.shape) != (B, K + 1):
+            raise ValueError(f"{what}: shapes hcat {tuple(hcat.shape)}, sel {tuple(sel.shape)}, gains "
+                             f"{tuple(gains.shape)} do not match topk={K}, F={F}, FS={self.FS}")
+        if sel.dtype != torch.int32 or gains.dtype != torch.float32:
+            raise TypeError(f"{what}: sel must be int32 and gains float32")
+        h_code = L.dtype_code(hcat, what)
+        if h_code == L.HSD_F32:
+            raise TypeError(f"{what}: hcat must be bf16 or f16")
+        dev = hcat.device
+        st = L.stream_of(hcat)
+        ib = self.inboxes
+        ws = L.ptr(ib.workspace)
+        if self.timing:
+            self._events = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        self._mark(0)
+        L.call("hsd_ep_dispatch", ws, self.rank, self.world, self.max_tokens, L.ptr(hcat), h_code, L.ptr(sel),
+               L.ptr(gains), B, K, F, self.FS, D, self.E, self.timeout_s, st)
+        self._mark(1)
+        y_shared = None
+        if self.shared_down is not None and B > 0:
+            y_shared = self.shared_down(hcat[:, K * F:].contiguous(), gains[:, K:]).contiguous()
+        self._mark(2)
+        L.call("hsd_ep_expert", ws, ctypes.c_void_p(ib.inbox), self.rank, self.world, self.max_tokens, L.ptr(self.pw),
+               L.ptr(self.ps), L.ptr(self.pb), self.s_code, h_code, K, F, D, self.E, self.timeout_s, st)
+        self._mark(3)
+        y = torch.empty((B, D), dtype=torch.float32, device=dev)
+        L.call("hsd_ep_combine", ws, self.rank, self.world, self.max_tokens, L.ptr(y_shared), L.ptr(y) if B else None,
+               B, K, F, D, self.E, self.timeout_s, st)
+        self._mark(4)
         return y

@@ -1,6 +1,8 @@
 """Expert-parallel dispatch / combine on CPU ranks (gloo, world size 2): the exchange logic of
-hsd_b200.ep (round-robin expert placement, one packed dispatch exchange) with the oracle's
-arithmetic standing in for the kernels, against the single-process oracle. No GPU."""
+hsd_b200.ep's collective form (round-robin expert placement, one packed dispatch exchange) with
+the oracle's arithmetic standing in for the kernels, against the single-process oracle; and the
+placement helpers the peer-memory form shares with it. No GPU (the peer-memory exchange runs in
+CUDA kernels: tests/test_ep_gpu.py)."""
 import os
 import socket
 
@@ -37,7 +39,7 @@ def _worker(rank, world, port, tokens_per_rank, q):
         from oracle import decode as od
         from oracle import layout as ol
         from oracle.quant import bf16_bits_to_f32, dequantize_neuron_major
-        from hsd_b200.ep import ExpertParallelDown
+        from hsd_b200.ep import ExpertParallelDownCollective
         c = _case()
         u16 = lambda t: t.view(torch.int16).numpy().view(np.uint16)  # noqa: E731
         w = c["w"].numpy().view(np.uint32)
@@ -53,7 +55,7 @@ def _worker(rank, world, port, tokens_per_rank, q):
         def shared_down(hs, g):
             return torch.from_numpy((hs.float().numpy() @ Wst).astype(np.float32)) * g
 
-        ep = ExpertParallelDown(E, F, FS, D, TOPK, group=None, local_down=local_down, shared_down=shared_down)
+        ep = ExpertParallelDownCollective(E, F, FS, D, TOPK, group=None, local_down=local_down, shared_down=shared_down)
         lo = sum(tokens_per_rank[:rank])
         hi = lo + tokens_per_rank[rank]
         y = ep(c["h"][lo:hi].contiguous(), c["sel"][lo:hi].contiguous(), c["gains"][lo:hi].contiguous())

@@ -1,6 +1,11 @@
-"""Expert-parallel down projection over 2 GPUs (NCCL): the same outputs as the single-GPU
-kernels on the same tokens, for batch decode (few slots per owner: the decode kernel) and a
-prefill chunk (many slots per owner: the tcgen05 GEMM). Needs 2 GPUs."""
+"""Expert-parallel down projection on GPUs: the peer-memory form (ExpertParallelDown: the
+hsd_ep_* kernels, inboxes mapped over CUDA IPC) and the collective baseline
+(ExpertParallelDownCollective, NCCL all_to_all) give the same outputs as the single-GPU
+operators on the same tokens, for batch decode rows and a prefill chunk, at world size 2 (needs
+2 GPUs) and at world size 1 (any GPU). A call of the peer-memory form reads nothing back to the
+host: it is captured in a CUDA graph and replayed. A bounded device-side wait that runs out
+(a flag no rank sets) returns HSD_ERR_TIMEOUT through the status word, with the context intact."""
+import ctypes
 import os
 import socket
 
@@ -21,6 +26,12 @@ def _free_port():
     return port
 
 
+def _single(hsd_b200, c, lo, hi, pw, ps, pb, spw, sps, spb):
+    args = (c["h"][lo:hi].contiguous(), c["sel"][lo:hi].contiguous(), c["gains"][lo:hi].contiguous(),
+            pw, ps, pb, spw, sps, spb)
+    return hsd_b200.sparse_down(*args, F=c["F"], FS=c["FS"], D=c["D"], topk=c["topk"], out_dtype=torch.float32)
+
+
 def _worker(rank, port, q):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
@@ -28,7 +39,7 @@ def _worker(rank, port, q):
         sys.path.insert(0, pth)
     import datetime
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
@@ -36,21 +47,30 @@ def _worker(rank, port, q):
     try:
         import hsd_b200
         from hsd_b200 import synth
-        from hsd_b200.ep import ExpertParallelDown, shard_experts
+        from hsd_b200.ep import ExpertParallelDown, ExpertParallelDownCollective, shard_experts
         out = []
+        inboxes = None
         for T in (8, 512):                  # batch decode rows, a prefill chunk, per rank
             c = synth.decode_case(seed=5, B=T * WORLD, zero_frac=0.9, device=dev, routing="zipf")
             pw, ps, pb = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"])
             spw, sps, spb = hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
-            ep = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"], *shard_experts(pw, ps, pb, rank, WORLD),
-                                    spw, sps, spb)
+            mine = shard_experts(pw, ps, pb, rank, WORLD)
             lo, hi = rank * T, (rank + 1) * T
-            y = ep(c["h"][lo:hi].contiguous(), c["sel"][lo:hi].contiguous(), c["gains"][lo:hi].contiguous())
-            ref = hsd_b200.sparse_down(c["h"][lo:hi].contiguous(), c["sel"][lo:hi].contiguous(),
-                                       c["gains"][lo:hi].contiguous(), pw, ps, pb, spw, sps, spb, F=c["F"],
-                                       FS=c["FS"], D=c["D"], topk=c["topk"], out_dtype=torch.float32)
+            # rank 1 brings one token fewer: B may differ between ranks
+            hi -= rank
+            x = (c["h"][lo:hi].contiguous(), c["sel"][lo:hi].contiguous(), c["gains"][lo:hi].contiguous())
+            ref = _single(hsd_b200, c, lo, hi, pw, ps, pb, spw, sps, spb)
+            p2p = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"], *mine, spw, sps, spb, max_tokens=512,
+                                     inboxes=inboxes)
+            inboxes = p2p.inboxes                # one inbox set for both shapes (and every layer)
+            ys = [p2p(*x) for _ in range(3)]     # three calls: epochs advance, buffers reused
+            coll = ExpertParallelDownCollective(c["E"], c["F"], c["FS"], c["D"], c["topk"], *mine, spw, sps, spb)
+            yc = coll(*x)
             torch.cuda.synchronize()
-            out.append((T, rel_err(y.cpu().numpy(), ref.cpu().numpy())))
+            r = ref.cpu().numpy()
+            out.append((T, [rel_err(y.cpu().numpy(), r) for y in ys], rel_err(yc.cpu().numpy(), r),
+                        all(torch.equal(ys[0], y) for y in ys), hsd_b200.device_status()))
+        inboxes.close()
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -71,27 +91,110 @@ def test_ep_two_gpus_matches_single_gpu(cuda):
         p.join(timeout=120)
         assert p.exitcode == 0
     for rank, out in res:
-        for T, err in out:
-            assert err < 5e-3, (rank, T, err)      # decode-kernel form exact to fp32 order; GEMM form fp16 operands
+        for T, errs, err_coll, same, status in out:
+            assert status == 0, (rank, T, status)
+            assert max(errs) < 5e-3, (rank, T, errs)   # GEMM form: fp16 operands, fp32 accumulation
+            assert err_coll < 5e-3, (rank, T, err_coll)
+            assert same, (rank, T)                       # repeated calls give the same bits
+
+
+def _case(cuda, T, seed=6):
+    import hsd_b200
+    from hsd_b200 import synth
+    c = synth.decode_case(seed=seed, B=T, zero_frac=0.9, device=cuda, routing="zipf")
+    pw, ps, pb = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"])
+    spw, sps, spb = hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
+    return c, (pw, ps, pb, spw, sps, spb)
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("T", [8, 512])
 def test_ep_one_gpu_path_matches_operator(cuda, T):
-    """The expert-parallel code path at world size 1 (no process group: the exchanges are local
-    copies, every expert local) equals the single-GPU operator on the same tokens: the packing,
-    the slot order, the per-slot kernels and the combine, on the hardware of a 1-GPU box."""
+    """Both forms at world size 1 (no process group: the rank's own inbox, every expert local)
+    equal the single-GPU operator on the same tokens."""
     import hsd_b200
-    from hsd_b200 import synth
-    from hsd_b200.ep import ExpertParallelDown
-    c = synth.decode_case(seed=6, B=T, zero_frac=0.9, device=cuda, routing="zipf")
-    pw, ps, pb = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"])
-    spw, sps, spb = hsd_b200.to_neuron_major(c["sw"], c["ss"], c["sb"])
-    ep = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"], pw, ps, pb, spw, sps, spb, timing=True)
+    from hsd_b200.ep import ExpertParallelDown, ExpertParallelDownCollective
+    c, wts = _case(cuda, T)
+    ref = _single(hsd_b200, c, 0, T, *wts).cpu().numpy()
+    ep = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"], *wts, max_tokens=512, timing=True)
     y = ep(c["h"], c["sel"], c["gains"])
-    ref = hsd_b200.sparse_down(c["h"], c["sel"], c["gains"], pw, ps, pb, spw, sps, spb, F=c["F"], FS=c["FS"],
-                               D=c["D"], topk=c["topk"], out_dtype=torch.float32)
-    torch.cuda.synchronize()
-    assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) < 5e-3
     ph = ep.phase_ms()
-    assert ph["total"] > 0 and set(ph) == {"dispatch", "compute", "combine", "total"}
+    coll = ExpertParallelDownCollective(c["E"], c["F"], c["FS"], c["D"], c["topk"], *wts, timing=True)
+    yc = coll(c["h"], c["sel"], c["gains"])
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), ref) < 5e-3
+    assert rel_err(yc.cpu().numpy(), ref) < 5e-3
+    assert ph["total"] > 0 and set(ph) == {"dispatch", "shared", "expert", "combine", "total"}
+    assert set(coll.phase_ms()) == {"dispatch", "compute", "combine", "total"}
+    assert hsd_b200.device_status() == 0
+    ep.inboxes.close()
+
+
+@pytest.mark.gpu
+def test_ep_call_replays_from_a_cuda_graph(cuda):
+    """The peer-memory call reads nothing back to the host, so it captures: replays of the graph
+    (each a new epoch of the flags) reproduce the eager call's bits on new inputs copied in."""
+    import hsd_b200
+    from hsd_b200.ep import ExpertParallelDown
+    T = 64
+    c, wts = _case(cuda, T, seed=8)
+    c2, _ = _case(cuda, T, seed=9)          # other tokens, same weights (seed of the weights differs: unused)
+    ep = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"], *wts, max_tokens=T)
+    h, sel, g = c["h"].clone(), c["sel"].clone(), c["gains"].clone()
+    ep(h, sel, g)                            # warm-up outside the capture
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            y_g = ep(h, sel, g)
+    torch.cuda.current_stream().wait_stream(s)
+    for src in (c, c2, c):
+        h.copy_(src["h"])
+        sel.copy_(src["sel"])
+        g.copy_(src["gains"])
+        graph.replay()
+        torch.cuda.synchronize()
+        y_e = ep(src["h"], src["sel"], src["gains"])
+        torch.cuda.synchronize()
+        assert torch.equal(y_g, y_e)
+    assert hsd_b200.device_status() == 0
+    del graph
+    ep.inboxes.close()
+
+
+@pytest.mark.gpu
+def test_ep_wait_for_a_missing_rank_times_out_with_status(cuda):
+    """A world of 2 whose second rank never runs: both inbox entries name this process's own
+    inbox, so every count row, row and arrival lands here -- but the count flag of rank 1 is
+    never set, and the dispatch's wait for it runs out (0.2 s). The call returns, the status
+    word says HSD_ERR_TIMEOUT, and the context stays usable."""
+    import hsd_b200
+    import hsd_b200._lib as L
+    c, wts = _case(cuda, 8, seed=7)
+    E, F, FS, D, K = c["E"], c["F"], c["FS"], c["D"], c["topk"]
+    assert hsd_b200.device_status() == 0
+    ib, wb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    L.call("hsd_ep_buffer_bytes", 2, 8, K, F, D, E, ctypes.byref(ib), ctypes.byref(wb))
+    p = ctypes.c_void_p(0)
+    L.call("hsd_ep_alloc", ib.value, ctypes.byref(p))
+    try:
+        ws = torch.empty(wb.value, dtype=torch.uint8, device=cuda)
+        table = (ctypes.c_uint64 * 2)(p.value, p.value)
+        st = L.stream_of(ws)
+        L.call("hsd_ep_set_peers", L.ptr(ws), ctypes.cast(table, ctypes.c_void_p), 2, st)
+        pw, ps, pb = (t[0::2].contiguous() for t in wts[:3])
+        y = torch.empty((8, D), dtype=torch.float32, device=cuda)
+        L.call("hsd_ep_dispatch", L.ptr(ws), 0, 2, 8, L.ptr(c["h"]), L.HSD_BF16, L.ptr(c["sel"]), L.ptr(c["gains"]),
+               8, K, F, FS, D, E, 0.2, st)
+        L.call("hsd_ep_expert", L.ptr(ws), p, 0, 2, 8, L.ptr(pw), L.ptr(ps), L.ptr(pb), L.HSD_BF16, L.HSD_BF16, K, F, D,
+               E, 0.2, st)
+        L.call("hsd_ep_combine", L.ptr(ws), 0, 2, 8, None, L.ptr(y), 8, K, F, D, E, 0.2, st)
+        torch.cuda.synchronize()
+        assert hsd_b200.device_status() == L.HSD_ERR_TIMEOUT
+        assert hsd_b200.device_status() == 0                    # read and cleared
+        torch.ones(4, device=cuda).sum().item()                 # the context still works
+    finally:
+        torch.cuda.synchronize()
+        L.call("hsd_ep_free", p)
