@@ -516,16 +516,16 @@ def ep_leg(layers, device, dist_on, reps=10):
         ms_coll = timed(lambda _: coll(h, sel, gains), reps, 3, device, dist_on) / reps
         y_coll, ph_coll = phases(coll, h, sel, gains)
         errs = [float((y_p2p - y_one).abs().max() / den), err_graph, float((y_coll - y_one).abs().max() / den)]
-        keys_p, keys_c = ("dispatch", "shared", "expert", "combine", "total"), ("dispatch", "compute", "combine", "total")
+        keys_p, keys_c = ("dispatch", "expert", "combine", "total"), ("dispatch", "compute", "combine", "total")
         v = max_ranks(errs + [ph_p2p[k] for k in keys_p] + [ph_coll[k] for k in keys_c])
         worst = max(worst, *v[:3])
         out[name] = {"ms": ms_graph, "tokens_per_s_all_ranks": world * T / (ms_graph / 1e3),
                      "tokens_per_s_per_gpu": T / (ms_graph / 1e3),
                      "eager_ms": ms_p2p, "eager_tokens_per_s_per_gpu": T / (ms_p2p / 1e3),
                      "rel_err": max(v[0], v[1]),
-                     "phases_ms_max_over_ranks": dict(zip(keys_p, v[3:8])),
+                     "phases_ms_max_over_ranks": dict(zip(keys_p, v[3:7])),
                      "collective_baseline": {"ms": ms_coll, "tokens_per_s_per_gpu": T / (ms_coll / 1e3),
-                                             "rel_err": v[2], "phases_ms_max_over_ranks": dict(zip(keys_c, v[8:12]))}}
+                                             "rel_err": v[2], "phases_ms_max_over_ranks": dict(zip(keys_c, v[7:11]))}}
     p2p.inboxes.close()
     out["gpus"] = world
     out["parity_ok"] = worst < 5e-3

@@ -4,7 +4,9 @@
  *
  * Every entry point takes plain device pointers, sizes and a cudaStream_t passed as
  * `void*`; none allocates, synchronises the device or reads back to the host, so all
- * of them are stream-ordered and can be captured in a CUDA graph. Every entry point
+ * of them are stream-ordered and can be captured in a CUDA graph -- except the one-time
+ * set-up calls of expert parallelism (hsd_ep_alloc / free / ipc_* / set_peers) and
+ * hsd_device_status, which say so. Every entry point
  * returns an hsd_status; on failure hsd_last_error_string() (thread-local) says why.
  * No entry point aborts the process and no kernel traps: a bad index met on the device
  * is skipped and recorded in a per-device status word read by hsd_device_status().
@@ -347,8 +349,8 @@ int hsd_sparse_down_prefill_noalloc(const void* h, int h_dtype, const float* gai
 #define HSD_EP_IPC_HANDLE_BYTES 64
 
 /* Bytes of a rank's inbox and of its private workspace (256-byte aligned, from any
- * allocator). At world 8, max_tokens 512 and the reference shapes: 124 MB and 100 MB. */
-int hsd_ep_buffer_bytes(int world, int max_tokens, int topk, int F, int D, int E,
+ * allocator). At world 8, max_tokens 512 and the reference shapes: 130 MB and 203 MB. */
+int hsd_ep_buffer_bytes(int world, int max_tokens, int topk, int F, int FS, int D, int E,
                         size_t* inbox_bytes, size_t* workspace_bytes);
 /* Zeroed device memory that other processes can map (cudaMalloc; free with hsd_ep_free).
  * The one allocation this library makes, and only here. */
@@ -369,17 +371,19 @@ int hsd_ep_set_peers(void* workspace, const uint64_t* inbox_addrs, int world, vo
 int hsd_ep_dispatch(void* workspace, int rank, int world, int max_tokens, const void* hcat,
                     int h_dtype, const int32_t* sel, const float* gains, int B, int topk, int F,
                     int FS, int D, int E, double timeout_s, void* stream);
-/* The owner's side: the slots this rank received times its experts pw [E/world, F, D/8],
- * ps / pb [E/world, F/64, D] (neuron-major, s_dtype bf16 or f16, owned_experts order) with
- * the tensor-core GEMM, each fp32 partial row times its gain stored into its home rank's
- * inbox. inbox: this rank's own inbox. */
+/* The GEMM side: the slots this rank received times its experts pw [E/world, F, D/8], ps / pb
+ * [E/world, F/64, D] (neuron-major, s_dtype bf16 or f16, owned_experts order), and the shared
+ * expert spw [FS, D/8], sps / spb [FS/64, D] of this rank's own B tokens (the same hcat as the
+ * dispatch), in one tensor-core GEMM launch; each fp32 partial row times its gain is stored
+ * into its home rank's inbox. inbox: this rank's own inbox. */
 int hsd_ep_expert(void* workspace, void* inbox, int rank, int world, int max_tokens,
-                  const uint32_t* pw, const void* ps, const void* pb, int s_dtype, int h_dtype,
-                  int topk, int F, int D, int E, double timeout_s, void* stream);
-/* y [B, D] f32 = the sum over each token's topk partial rows in slot order, + y_shared [B, D]
- * f32 when given (the shared expert of the same tokens, computed by the caller). */
-int hsd_ep_combine(void* workspace, int rank, int world, int max_tokens, const float* y_shared,
-                   float* y, int B, int topk, int F, int D, int E, double timeout_s, void* stream);
+                  const void* hcat, int h_dtype, int B, const uint32_t* pw, const void* ps,
+                  const void* pb, const uint32_t* spw, const void* sps, const void* spb,
+                  int s_dtype, int topk, int F, int FS, int D, int E, double timeout_s, void* stream);
+/* y [B, D] f32 = the sum over each token's topk partial rows in slot order, then its shared
+ * expert row (FS > 0). */
+int hsd_ep_combine(void* workspace, int rank, int world, int max_tokens, float* y, int B,
+                   int topk, int F, int FS, int D, int E, double timeout_s, void* stream);
 
 #ifdef __cplusplus
 }

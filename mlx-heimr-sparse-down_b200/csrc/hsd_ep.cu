@@ -13,9 +13,10 @@
 //              cnt[s][d]    slots source s sends to rank d        (every source writes its row everywhere)
 //   h_in       [R][F]       the slots this rank owns: h rows      (R = G * S receive capacity,
 //   sel_in     [R]          ... local expert id                    S = max_tokens * topk)
-//   g_in       [R][2]       ... routing gain, 0
+//   g_in       [R][2]       ... routing gain; [t][1]: this rank's token t's shared-expert gain
 //   ret_in     [R]          ... source rank * S + source slot
-//   ysl        [S][D] f32   this rank's slots' partial rows, written by their owners
+//   ysl        [S+T][D] f32 this rank's slots' partial rows, written by their owners, then its
+//                           tokens' shared-expert rows (T = max_tokens), written by itself
 //
 // One call, all on the caller's stream (every rank makes the same calls in the same order):
 //   hsd_ep_dispatch  route: per-slot destination and stable position, the count row to every
@@ -24,11 +25,12 @@
 //                    base(src -> owner) + position; arrivals counted on the owner
 //   hsd_ep_expert    wait for every source's scatter CTAs; the received rows' return addresses;
 //                    the expert-sorted tile order over the R received rows (count read on the
-//                    device); the tcgen05 grouped GEMM whose epilogue stores each fp32 partial
-//                    row, times its gain, straight into the home rank's ysl row (over NVLink);
-//                    then one arrival on every rank
-//   hsd_ep_combine   wait for the G owners; y[b] = sum_k ysl[b*topk + k] (+ the caller's
-//                    shared-expert rows), fixed order
+//                    device) followed by the shared expert's tiles of this rank's own tokens;
+//                    ONE tcgen05 grouped GEMM over both, whose epilogue stores each fp32 partial
+//                    row, times its gain, straight into its home rank's ysl row (over NVLink;
+//                    the shared rows into this rank's own); then one arrival on every rank
+//   hsd_ep_combine   wait for the G owners; y[b] = sum_k ysl[b*topk + k] + ysl[S + b], fixed
+//                    order
 // Nothing is read back to the host, so the call can be captured in a CUDA graph. The counters
 // are cumulative (compared modulo 2^32), so no buffer is ever reset. A rank reaches call n+1
 // only after its combine of call n has seen every owner's arrival, which every owner sends
@@ -62,20 +64,22 @@ constexpr size_t kHdrBytes = 4096;
 constexpr size_t up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct EpLayout {
-  int G, S, R, F, D, E_local, NT, mrb;
+  int G, S, R, T, F, FS, D, E_local, NT_routed, NT, kmax, mrb;
   // inbox offsets
   size_t h_in, sel_in, g_in, ret_in, ysl, inbox_bytes;
   // workspace offsets
   size_t w_peers, w_misc, w_pos, w_te, w_ts, w_km, w_hc, w_rowdst, ws_bytes;
 };
 
-int ep_layout(int world, int max_tokens, int topk, int F, int D, int E, EpLayout* L) {
+int ep_layout(int world, int max_tokens, int topk, int F, int FS, int D, int E, EpLayout* L) {
   if (world < 1 || world > kMaxWorld)
     return hsd::set_error(HSD_ERR_SHAPE, "ep: world %d outside 1..%d", world, kMaxWorld);
-  if (max_tokens < 1 || topk < 1 || F < 64 || F % 64 != 0 || D < 192 || D % 192 != 0 || E < 1 || E % world != 0)
+  if (max_tokens < 1 || topk < 1 || F < 64 || F % 64 != 0 || FS < 0 || FS % 64 != 0 || D < 192 || D % 192 != 0 ||
+      E < 1 || E % world != 0)
     return hsd::set_error(HSD_ERR_SHAPE,
-                          "ep: need max_tokens, topk >= 1, F %% 64 == 0, D %% 192 == 0, E %% world == 0 "
-                          "(max_tokens=%d topk=%d F=%d D=%d E=%d world=%d)", max_tokens, topk, F, D, E, world);
+                          "ep: need max_tokens, topk >= 1, F and FS %% 64 == 0, D %% 192 == 0, E %% world == 0 "
+                          "(max_tokens=%d topk=%d F=%d FS=%d D=%d E=%d world=%d)", max_tokens, topk, F, FS, D, E,
+                          world);
   const long long S = static_cast<long long>(max_tokens) * topk;
   if (S >= (1ll << 24) || S * world >= (1ll << 27))
     return hsd::set_error(HSD_ERR_SHAPE, "ep: max_tokens * topk * world too large (%lld slots)", S * world);
@@ -83,21 +87,25 @@ int ep_layout(int world, int max_tokens, int topk, int F, int D, int E, EpLayout
   L->G = world;
   L->S = static_cast<int>(S);
   L->R = static_cast<int>(S * world);
+  L->T = max_tokens;
   L->F = F;
+  L->FS = FS;
   L->D = D;
   L->E_local = E / world;
   int nr = 0, ns = 0;
   int rc = hsd::prefill_tile_counts(L->R, 1, L->E_local, hsd::kPrefillTile, &nr, &ns);
   if (rc) return rc;
-  L->NT = nr;                                        // routed tiles only: the shared expert stays home
-  L->mrb = hsd::mask_row_bytes(F);
+  L->NT_routed = nr;                                 // then the shared expert's tiles of this rank's tokens
+  L->NT = nr + (FS > 0 ? (max_tokens + hsd::kPrefillTile - 1) / hsd::kPrefillTile : 0);
+  L->kmax = F > FS ? F : FS;
+  L->mrb = hsd::mask_row_bytes(L->kmax);
   const size_t R = static_cast<size_t>(L->R);
   L->h_in = kHdrBytes;
   L->sel_in = up(L->h_in + R * F * 2, 256);
   L->g_in = up(L->sel_in + R * 4, 256);
   L->ret_in = up(L->g_in + R * 8, 256);
   L->ysl = up(L->ret_in + R * 4, 256);
-  L->inbox_bytes = L->ysl + static_cast<size_t>(L->S) * D * 4;
+  L->inbox_bytes = L->ysl + (static_cast<size_t>(L->S) + max_tokens) * D * 4;
   const size_t NT = static_cast<size_t>(L->NT);
   L->w_peers = 0;
   L->w_misc = 256;
@@ -106,7 +114,7 @@ int ep_layout(int world, int max_tokens, int topk, int F, int D, int E, EpLayout
   L->w_ts = up(L->w_te + NT * 4, 256);
   L->w_km = up(L->w_ts + NT * hsd::kPrefillTile * 4, 256);
   L->w_hc = up(L->w_km + NT * L->mrb, 256);
-  L->w_rowdst = up(L->w_hc + NT * hsd::kPrefillTile * F * 2, 256);
+  L->w_rowdst = up(L->w_hc + NT * hsd::kPrefillTile * L->kmax * 2, 256);
   L->ws_bytes = L->w_rowdst + R * 8;
   return HSD_OK;
 }
@@ -210,15 +218,17 @@ __global__ void __launch_bounds__(kRouteThreads) ep_route_kernel(const uint64_t*
 
 // ---- scatter (kScatterCTAs CTAs): once the G count rows of this epoch are in, each slot's h
 //      row (16-byte pieces, one warp a slot), local expert id, gain and return address go to
-//      row base(rank -> owner) + position of the owner's inbox; then every CTA counts one
-//      arrival on every rank.
+//      row base(rank -> owner) + position of the owner's inbox; this rank's tokens'
+//      shared-expert gains go to its own inbox (g_in[t][1]); then every CTA counts one arrival
+//      on every rank.
 __global__ void __launch_bounds__(kScatterThreads) ep_scatter_kernel(const uint64_t* __restrict__ peers, int rank,
                                                                      int G, int S, const unsigned char* __restrict__ hcat,
                                                                      const int32_t* __restrict__ sel,
                                                                      const float* __restrict__ gains,
                                                                      const int32_t* __restrict__ pos, int nslots,
-                                                                     int topk, int F, int NR, int E, InboxOffsets off,
+                                                                     int topk, int F, int FS, int E, InboxOffsets off,
                                                                      unsigned long long timeout_ns) {
+  const int NR = topk * F + FS;
   __shared__ int base[kMaxWorld];
   __shared__ int ok_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -252,10 +262,16 @@ __global__ void __launch_bounds__(kScatterThreads) ep_scatter_kernel(const uint6
       if (lane == 0) {
         const int e = sel[j];
         reinterpret_cast<int32_t*>(dst + off.sel_in)[row] = (e >= 0 && e < E) ? e / G : -1;
-        reinterpret_cast<float2*>(dst + off.g_in)[row] = make_float2(gains[static_cast<int64_t>(b) * (topk + 1) + k], 0.f);
+        reinterpret_cast<float*>(dst + off.g_in)[2 * static_cast<int64_t>(row)] =
+            gains[static_cast<int64_t>(b) * (topk + 1) + k];
         reinterpret_cast<int32_t*>(dst + off.ret_in)[row] = rank * S + j;
       }
     }
+  }
+  if (FS > 0) {                                    // (g_in[t][1] of a received row is never read)
+    float* own_g = reinterpret_cast<float*>(inbox(peers, rank) + off.g_in);
+    for (int t = blockIdx.x * kScatterThreads + tid; t < nslots / topk; t += gridDim.x * kScatterThreads)
+      own_g[2 * static_cast<int64_t>(t) + 1] = gains[static_cast<int64_t>(t) * (topk + 1) + topk];
   }
   __threadfence_system();
   __syncthreads();
@@ -303,11 +319,11 @@ __global__ void ep_signal_kernel(const uint64_t* __restrict__ peers, int G) {
     red_add_release_sys(reinterpret_cast<uint32_t*>(inbox(peers, threadIdx.x) + kOffArrY), 1u);
 }
 
-// ---- combine: wait for the G owners, then y[b] = sum_k ysl[b*topk + k] (+ y_shared[b]).
+// ---- combine: wait for the G owners, then y[b] = sum_k ysl[b*topk + k] (+ ysl[S + b], the
+//      shared expert's row, when there is one).
 __global__ void __launch_bounds__(kCombineThreads) ep_combine_kernel(const uint64_t* __restrict__ peers, int rank, int G,
-                                                                     int B, int topk, int D, InboxOffsets off,
-                                                                     const float* __restrict__ y_shared,
-                                                                     float* __restrict__ y,
+                                                                     int B, int topk, int S, int shared, int D,
+                                                                     InboxOffsets off, float* __restrict__ y,
                                                                      unsigned long long timeout_ns) {
   __shared__ int ok_s;
   if (threadIdx.x == 0) {
@@ -332,8 +348,8 @@ __global__ void __launch_bounds__(kCombineThreads) ep_combine_kernel(const uint6
       a.z += v.z;
       a.w += v.w;
     }
-    if (y_shared) {
-      const float4 v = reinterpret_cast<const float4*>(y_shared)[i];
+    if (shared && ok_s) {
+      const float4 v = ysl[(static_cast<int64_t>(S) + b) * D4 + o];
       a.x += v.x;
       a.y += v.y;
       a.z += v.z;
@@ -370,11 +386,11 @@ int check_rank(int rank, int world, const void* ws) {
 
 // ---- C ABI -------------------------------------------------------------------------------
 
-extern "C" int hsd_ep_buffer_bytes(int world, int max_tokens, int topk, int F, int D, int E, size_t* inbox_bytes,
-                                   size_t* workspace_bytes) {
+extern "C" int hsd_ep_buffer_bytes(int world, int max_tokens, int topk, int F, int FS, int D, int E,
+                                   size_t* inbox_bytes, size_t* workspace_bytes) {
   if (!inbox_bytes || !workspace_bytes) return hsd::set_error(HSD_ERR_ARG, "hsd_ep_buffer_bytes: null output");
   EpLayout L;
-  int rc = ep_layout(world, max_tokens, topk, F, D, E, &L);
+  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, &L);
   if (rc) return rc;
   *inbox_bytes = L.inbox_bytes;
   *workspace_bytes = L.ws_bytes;
@@ -441,7 +457,7 @@ extern "C" int hsd_ep_dispatch(void* workspace, int rank, int world, int max_tok
                                const int32_t* sel, const float* gains, int B, int topk, int F, int FS, int D, int E,
                                double timeout_s, void* stream) {
   EpLayout L;
-  int rc = ep_layout(world, max_tokens, topk, F, D, E, &L);
+  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, &L);
   if (rc) return rc;
   if ((rc = check_rank(rank, world, workspace))) return rc;
   if (B < 0 || B > max_tokens)
@@ -449,7 +465,6 @@ extern "C" int hsd_ep_dispatch(void* workspace, int rank, int world, int max_tok
   if (B > 0 && (!hcat || !sel || !gains)) return hsd::set_error(HSD_ERR_ARG, "hsd_ep_dispatch: null pointer");
   if (h_dtype != HSD_BF16 && h_dtype != HSD_F16)
     return hsd::set_error(HSD_ERR_DTYPE, "hsd_ep_dispatch: h_dtype %d (bf16 or f16)", h_dtype);
-  if (FS < 0 || FS % 64 != 0) return hsd::set_error(HSD_ERR_SHAPE, "hsd_ep_dispatch: FS %% 64 != 0");
   if (hcat && !hsd::aligned(hcat, 16)) return hsd::set_error(HSD_ERR_ALIGN, "hsd_ep_dispatch: hcat must be 16-byte aligned");
   cudaStream_t st = hsd::as_stream(stream);
   unsigned char* ws = static_cast<unsigned char*>(workspace);
@@ -459,24 +474,29 @@ extern "C" int hsd_ep_dispatch(void* workspace, int rank, int world, int max_tok
   if ((rc = hsd::check_launch("hsd_ep_dispatch: route"))) return rc;
   ep_scatter_kernel<<<kScatterCTAs, kScatterThreads, 0, st>>>(peers, rank, world, L.S,
                                                               static_cast<const unsigned char*>(hcat), sel, gains, pos,
-                                                              B * topk, topk, F, topk * F + FS, E, offsets_of(L),
+                                                              B * topk, topk, F, FS, E, offsets_of(L),
                                                               timeout_ns_of(timeout_s));
   return hsd::check_launch("hsd_ep_dispatch: scatter");
 }
 
-extern "C" int hsd_ep_expert(void* workspace, void* inbox_ptr, int rank, int world, int max_tokens, const uint32_t* pw,
-                             const void* ps, const void* pb, int s_dtype, int h_dtype, int topk, int F, int D, int E,
-                             double timeout_s, void* stream) {
+extern "C" int hsd_ep_expert(void* workspace, void* inbox_ptr, int rank, int world, int max_tokens, const void* hcat,
+                             int h_dtype, int B, const uint32_t* pw, const void* ps, const void* pb,
+                             const uint32_t* spw, const void* sps, const void* spb, int s_dtype, int topk, int F, int FS,
+                             int D, int E, double timeout_s, void* stream) {
   EpLayout L;
-  int rc = ep_layout(world, max_tokens, topk, F, D, E, &L);
+  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, &L);
   if (rc) return rc;
   if ((rc = check_rank(rank, world, workspace))) return rc;
-  if (!inbox_ptr || !pw || !ps || !pb) return hsd::set_error(HSD_ERR_ARG, "hsd_ep_expert: null pointer");
+  if (B < 0 || B > max_tokens)
+    return hsd::set_error(HSD_ERR_SHAPE, "hsd_ep_expert: B=%d outside 0..max_tokens=%d", B, max_tokens);
+  if (!inbox_ptr || !pw || !ps || !pb || (FS > 0 && (!spw || !sps || !spb)) || (FS > 0 && B > 0 && !hcat))
+    return hsd::set_error(HSD_ERR_ARG, "hsd_ep_expert: null pointer");
   if (h_dtype != HSD_BF16 && h_dtype != HSD_F16)
     return hsd::set_error(HSD_ERR_DTYPE, "hsd_ep_expert: h_dtype %d (bf16 or f16)", h_dtype);
-  const void* p16[] = {pw, ps, pb, inbox_ptr};
+  const void* p16[] = {pw, ps, pb, spw, sps, spb, inbox_ptr, hcat};
   for (const void* q : p16)
-    if (!hsd::aligned(q, 16)) return hsd::set_error(HSD_ERR_ALIGN, "hsd_ep_expert: weights and inbox must be 16-byte aligned");
+    if (!hsd::aligned(q, 16))
+      return hsd::set_error(HSD_ERR_ALIGN, "hsd_ep_expert: weights, inbox and hcat must be 16-byte aligned");
   cudaStream_t st = hsd::as_stream(stream);
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   unsigned char* ib = static_cast<unsigned char*>(inbox_ptr);
@@ -489,28 +509,36 @@ extern "C" int hsd_ep_expert(void* workspace, void* inbox_ptr, int rank, int wor
   float** row_dst = reinterpret_cast<float**>(ws + L.w_rowdst);
   ep_recv_kernel<<<1, 1024, 0, st>>>(peers, rank, world, L.S, D, offsets_of(L), nrecv, row_dst, timeout_ns_of(timeout_s));
   if ((rc = hsd::check_launch("hsd_ep_expert: receive"))) return rc;
+  // this call's tiles: the routed ones (fixed count for the capacity), then ceil(B / 128) of
+  // the shared expert over this rank's B tokens
+  const int ns = (FS > 0) ? (B + hsd::kPrefillTile - 1) / hsd::kPrefillTile : 0;
+  const int NT = L.NT_routed + ns;
   const int32_t* sel_in = reinterpret_cast<const int32_t*>(ib + L.sel_in);
-  if ((rc = hsd::launch_build_tiles(sel_in, L.R, 1, L.E_local, hsd::kPrefillTile, L.NT, 0, nrecv, te, ts, st))) return rc;
-  if ((rc = hsd::launch_gather(ib + L.h_in, h_dtype, te, ts, L.NT, hsd::kPrefillTile, F, 0, 1, L.E_local, F, hc, km, st)))
+  if ((rc = hsd::launch_build_tiles(sel_in, L.R, 1, L.E_local, hsd::kPrefillTile, L.NT_routed, ns, B, nrecv, te, ts, st)))
     return rc;
-  rc = hsd::launch_prefill_gemm(hc, F, te, ts, L.NT, km, reinterpret_cast<const float*>(ib + L.g_in), pw, ps, pb, s_dtype,
-                                nullptr, nullptr, nullptr, nullptr, L.R, D, F, 0, 1, L.E_local, st, row_dst);
+  const int esz = 2;
+  const void* hs = (FS > 0 && hcat) ? static_cast<const unsigned char*>(hcat) + static_cast<int64_t>(topk) * F * esz : nullptr;
+  rc = hsd::launch_gather(ib + L.h_in, h_dtype, te, ts, NT, hsd::kPrefillTile, F, FS, 1, L.E_local, L.kmax, hc, km, st,
+                          hs ? hs : ib + L.h_in, static_cast<int64_t>(topk) * F + FS, F);
+  if (rc) return rc;
+  float* shared_out = reinterpret_cast<float*>(ib + L.ysl) + static_cast<int64_t>(L.S) * D;
+  rc = hsd::launch_prefill_gemm(hc, L.kmax, te, ts, NT, km, reinterpret_cast<const float*>(ib + L.g_in), pw, ps, pb,
+                                s_dtype, spw, sps, spb, nullptr, L.R, D, F, FS, 1, L.E_local, st, row_dst, shared_out);
   if (rc) return rc;
   ep_signal_kernel<<<1, 32, 0, st>>>(peers, world);
   return hsd::check_launch("hsd_ep_expert: signal");
 }
 
-extern "C" int hsd_ep_combine(void* workspace, int rank, int world, int max_tokens, const float* y_shared, float* y,
-                              int B, int topk, int F, int D, int E, double timeout_s, void* stream) {
+extern "C" int hsd_ep_combine(void* workspace, int rank, int world, int max_tokens, float* y, int B, int topk, int F,
+                              int FS, int D, int E, double timeout_s, void* stream) {
   EpLayout L;
-  int rc = ep_layout(world, max_tokens, topk, F, D, E, &L);
+  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, &L);
   if (rc) return rc;
   if ((rc = check_rank(rank, world, workspace))) return rc;
   if (B < 0 || B > max_tokens)
     return hsd::set_error(HSD_ERR_SHAPE, "hsd_ep_combine: B=%d outside 0..max_tokens=%d", B, max_tokens);
   if (B > 0 && !y) return hsd::set_error(HSD_ERR_ARG, "hsd_ep_combine: null output");
-  if ((y && !hsd::aligned(y, 16)) || (y_shared && !hsd::aligned(y_shared, 16)))
-    return hsd::set_error(HSD_ERR_ALIGN, "hsd_ep_combine: y and y_shared must be 16-byte aligned");
+  if (y && !hsd::aligned(y, 16)) return hsd::set_error(HSD_ERR_ALIGN, "hsd_ep_combine: y must be 16-byte aligned");
   cudaStream_t st = hsd::as_stream(stream);
   const uint64_t* peers = reinterpret_cast<const uint64_t*>(static_cast<unsigned char*>(workspace) + L.w_peers);
   // (launched with B = 0 too: its wait orders this rank's next dispatch after every owner's reads)
@@ -518,7 +546,7 @@ extern "C" int hsd_ep_combine(void* workspace, int rank, int world, int max_toke
   long long grid = (n4 + kCombineThreads - 1) / kCombineThreads;
   if (grid < 1) grid = 1;
   if (grid > 4 * 148) grid = 4 * 148;
-  ep_combine_kernel<<<static_cast<unsigned>(grid), kCombineThreads, 0, st>>>(peers, rank, world, B, topk, D, offsets_of(L),
-                                                                           y_shared, y, timeout_ns_of(timeout_s));
+  ep_combine_kernel<<<static_cast<unsigned>(grid), kCombineThreads, 0, st>>>(peers, rank, world, B, topk, L.S, FS > 0 ? 1 : 0,
+                                                                           D, offsets_of(L), y, timeout_ns_of(timeout_s));
   return hsd::check_launch("hsd_ep_combine");
 }

@@ -26,7 +26,7 @@ constexpr int kMaxExperts = 256;
 // (warp match). Then the slot scatter and the tile experts.
 __global__ void __launch_bounds__(kTileThreads) build_tiles_kernel(const int32_t* __restrict__ sel,
                                                                    int T, int topk, int E, int tt,
-                                                                   int nt_routed, int nt_shared,
+                                                                   int nt_routed, int nt_shared, int T_shared,
                                                                    const int* __restrict__ nslots_dev,
                                                                    int32_t* __restrict__ tile_e,
                                                                    int32_t* __restrict__ tile_slot) {
@@ -91,10 +91,10 @@ __global__ void __launch_bounds__(kTileThreads) build_tiles_kernel(const int32_t
     }
     __syncthreads();
   }
-  // the shared expert's tiles: tokens in order
+  // the shared expert's tiles: tokens 0 .. T_shared-1 in order
   for (int i = tid; i < nt_shared; i += kTileThreads) tile_e[nt_routed + i] = E;
   for (int i = tid; i < nt_shared * tt; i += kTileThreads)
-    tile_slot[nt_routed * tt + i] = (i < T) ? i : -1;
+    tile_slot[nt_routed * tt + i] = (i < T_shared) ? i : -1;
 }
 
 // Union of live columns per tile (hsd/prefill.py:48-93): one CTA per tile; thread-per-column
@@ -156,24 +156,26 @@ __global__ void __launch_bounds__(256) build_union_kernel(const HT* __restrict__
 
 // A operand: hc[tile*tt + m, c] = fp16(h[slot's columns][c]), c < the tile's K, zero rows for
 // padding slots; 8 columns (one 16-byte store) per thread. Rows of empty tiles are skipped.
+// Routed slot t*topk + k reads h[t * h_stride + k*F + c]; the shared expert's row of token t
+// reads hs[t * hs_stride + c].
 // One CTA per (64-column group, tile): its 128 A rows' 64 columns as fp16 (8 lanes a row, 16
 // bytes a lane, coalesced both ways), and one byte of the tile's live-K-tile mask,
 // kmask[tile][group] = 1 iff any of them is nonzero (rows of mask_row_bytes(kmax) bytes) --
 // the tensor-core GEMM skips the K-tiles whose byte is 0 (only zeros to multiply). Every byte a
 // non-empty tile's GEMM uses is written here, so the mask needs no clearing.
 template <typename HT>
-__global__ void __launch_bounds__(256) gather_kernel(const HT* __restrict__ h,
+__global__ void __launch_bounds__(256) gather_kernel(const HT* __restrict__ h, int64_t h_stride,
                                                      const int32_t* __restrict__ tile_e,
                                                      const int32_t* __restrict__ tile_slot, int tt,
                                                      int F, int FS, int topk, int E, int kmax,
-                                                     __half* __restrict__ hc, uint8_t* __restrict__ kmask) {
+                                                     __half* __restrict__ hc, uint8_t* __restrict__ kmask,
+                                                     const HT* __restrict__ hs, int64_t hs_stride) {
   const int grp = blockIdx.x, tile = blockIdx.y;
   const int e = tile_e[tile];
   if (e < 0) return;
   const bool shared = e >= E;
   const int FF = shared ? FS : F;
   const int c8 = grp * 64 + (threadIdx.x & 7) * 8;
-  const int64_t NR = static_cast<int64_t>(topk) * F + FS;
   bool nz = false;
   if (grp * 64 < FF) {
     for (int r = threadIdx.x >> 3; r < tt; r += 32) {
@@ -184,11 +186,11 @@ __global__ void __launch_bounds__(256) gather_kernel(const HT* __restrict__ h,
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = __float2half_rn(0.f);
       } else {
-        const int64_t o = (shared ? s * NR + static_cast<int64_t>(topk) * F
-                                  : (s / topk) * NR + static_cast<int64_t>(s % topk) * F) + c8;
+        const HT* src = shared ? hs + s * hs_stride + c8
+                               : h + (s / topk) * h_stride + static_cast<int64_t>(s % topk) * F + c8;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          v[i] = __float2half_rn(hsd::to_f32<HT>(h[o + i]));
+          v[i] = __float2half_rn(hsd::to_f32<HT>(src[i]));
           nz |= (__half_as_ushort(v[i]) & 0x7FFFu) != 0u;
         }
       }
@@ -231,29 +233,38 @@ int prefill_tile_counts(int T, int topk, int E, int tt, int* nt_routed, int* nt_
 }
 
 int launch_build_tiles(const int32_t* sel, int T, int topk, int E, int tt, int nt_routed, int nt_shared,
-                       const int* nslots_dev, int32_t* tile_e, int32_t* tile_slot, cudaStream_t st) {
+                       int T_shared, const int* nslots_dev, int32_t* tile_e, int32_t* tile_slot, cudaStream_t st) {
   if (E > kMaxExperts) return set_error(HSD_ERR_SHAPE, "prefill build_tiles: E > %d", kMaxExperts);
   if (static_cast<long long>(T) * topk > (1ll << 30)) return set_error(HSD_ERR_SHAPE, "prefill build_tiles: too many slots");
-  build_tiles_kernel<<<1, kTileThreads, 0, st>>>(sel, T, topk, E, tt, nt_routed, nt_shared, nslots_dev, tile_e,
-                                                 tile_slot);
+  build_tiles_kernel<<<1, kTileThreads, 0, st>>>(sel, T, topk, E, tt, nt_routed, nt_shared, T_shared, nslots_dev,
+                                                 tile_e, tile_slot);
   return check_launch("prefill build_tiles");
 }
 
 int launch_gather(const void* h, int h_dtype, const int32_t* tile_e, const int32_t* tile_slot, int NT,
-                  int tt, int F, int FS, int topk, int E, int kmax, __half* hc, uint8_t* kmask, cudaStream_t st) {
+                  int tt, int F, int FS, int topk, int E, int kmax, __half* hc, uint8_t* kmask, cudaStream_t st,
+                  const void* hs, int64_t hs_stride, int64_t h_stride) {
   const dim3 grid(static_cast<unsigned>(kmax / 64), static_cast<unsigned>(NT));
+  if (h_stride <= 0) h_stride = static_cast<int64_t>(topk) * F + FS;
+  const int esz = h_dtype == HSD_F32 ? 4 : 2;
+  if (!hs) {
+    hs = static_cast<const unsigned char*>(h) + static_cast<int64_t>(topk) * F * esz;
+    hs_stride = static_cast<int64_t>(topk) * F + FS;
+  }
   switch (h_dtype) {
     case HSD_F32:
-      gather_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(h), tile_e, tile_slot, tt, F, FS,
-                                                 topk, E, kmax, hc, kmask);
+      gather_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(h), h_stride, tile_e, tile_slot, tt, F, FS,
+                                                 topk, E, kmax, hc, kmask, static_cast<const float*>(hs), hs_stride);
       break;
     case HSD_F16:
-      gather_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(h), tile_e, tile_slot, tt, F, FS,
-                                                  topk, E, kmax, hc, kmask);
+      gather_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(h), h_stride, tile_e, tile_slot, tt, F,
+                                                  FS, topk, E, kmax, hc, kmask, static_cast<const __half*>(hs),
+                                                  hs_stride);
       break;
     case HSD_BF16:
-      gather_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(h), tile_e,
-                                                         tile_slot, tt, F, FS, topk, E, kmax, hc, kmask);
+      gather_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(h), h_stride, tile_e,
+                                                         tile_slot, tt, F, FS, topk, E, kmax, hc, kmask,
+                                                         static_cast<const __nv_bfloat16*>(hs), hs_stride);
       break;
     default: return set_error(HSD_ERR_DTYPE, "prefill gather: h_dtype %d", h_dtype);
   }
@@ -288,7 +299,7 @@ extern "C" int hsd_prefill_build_tiles(const int32_t* sel, int T, int topk, int 
   int nr = 0, ns = 0;
   int rc = hsd::prefill_tile_counts(T, topk, E, tt, &nr, &ns);
   if (rc) return rc;
-  return hsd::launch_build_tiles(sel, T, topk, E, tt, nr, ns, nullptr, tile_e, tile_slot, hsd::as_stream(stream));
+  return hsd::launch_build_tiles(sel, T, topk, E, tt, nr, ns, T, nullptr, tile_e, tile_slot, hsd::as_stream(stream));
 }
 
 extern "C" int hsd_prefill_build_union(const void* h, int h_dtype, const int32_t* tile_e, const int32_t* tile_slot,

@@ -90,7 +90,8 @@ struct GemmParams {
   const uint16_t* sps;
   const uint16_t* spb;
   float* part;
-  float* const* row_dst;   // optional: slot s's output row is row_dst[s] (another GPU's memory allowed), not part
+  float* const* row_dst;   // optional: routed slot s's output row is row_dst[s] (another GPU's memory allowed)
+  float* shared_out;       // optional: the shared expert's row of token t is shared_out + t * D
   const uint8_t* kmask;    // [NT][KG] live-K-tile bytes from the gather (KG: kmax / 64 rounded up to 8)
   int NT, T, D, F, FS, topk, E, nnt, KG;
 };
@@ -362,7 +363,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         row = (e >= p.E) ? static_cast<int64_t>(s) * (p.topk + 1) + p.topk
                          : static_cast<int64_t>(s / p.topk) * (p.topk + 1) + (s % p.topk);
         g = __ldg(p.gains + row);
-        out_row = p.row_dst ? p.row_dst[s] : p.part + row * p.D;
+        out_row = (e >= p.E) ? (p.shared_out ? p.shared_out + static_cast<int64_t>(s) * p.D : p.part + row * p.D)
+                             : (p.row_dst ? p.row_dst[s] : p.part + row * p.D);
       }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(acc) * ACC_COLS;
 #pragma unroll 1
@@ -551,7 +553,8 @@ namespace hsd {
 int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const int32_t* tile_slot, int NT,
                         const uint8_t* kmask, const float* gains, const uint32_t* pw, const void* ps, const void* pb, int s_dtype,
                         const uint32_t* spw, const void* sps, const void* spb, float* part, int T, int D,
-                        int F, int FS, int topk, int E, cudaStream_t st, float* const* row_dst) {
+                        int F, int FS, int topk, int E, cudaStream_t st, float* const* row_dst,
+                        float* shared_out) {
   if (D % BN != 0 || F % BK != 0 || FS < 0 || FS % BK != 0 || kmax % BK != 0)
     return set_error(HSD_ERR_SHAPE, "prefill gemm: need D %% %d == 0, F and FS %% 64 == 0 (D=%d F=%d FS=%d)", BN,
                      D, F, FS);
@@ -580,6 +583,7 @@ int launch_prefill_gemm(const __half* hc, int kmax, const int32_t* tile_e, const
   p.spb = static_cast<const uint16_t*>(spb);
   p.part = part;
   p.row_dst = row_dst;
+  p.shared_out = shared_out;
   p.kmask = kmask;
   p.KG = (kmax / BK + 7) / 8 * 8;
   p.NT = NT;

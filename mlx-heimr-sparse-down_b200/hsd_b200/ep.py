@@ -17,8 +17,9 @@ rank's process and written with plain stores over NVLink, ordered by release / a
             inbox (the counts travel the same way first, so nothing is read back to the host)
   expert    the owner runs the tcgen05 grouped GEMM over the rows it received; the epilogue
             stores each fp32 partial row, times its gain, into its home rank's inbox
-  combine   the home rank sums each token's topk partials in slot order plus its own
-            shared-expert rows (computed between dispatch and expert, while the rows travel)
+  combine   the home rank sums each token's topk partials in slot order plus its shared-expert
+            row (the owner's GEMM launch also runs the shared expert's tiles of the rank's own
+            tokens, so one persistent grid covers both)
 
 The partials stay fp32: six bf16-rounded partials per token would cost ~2^-9 relative each,
 most of the parity budget. With one GPU the same path runs with the rank's own inbox.
@@ -194,13 +195,13 @@ class PeerInboxes:
     synchronises the device, waits for every rank, unmaps the peers' inboxes and frees this
     rank's; without it the memory stays until the process exits."""
 
-    def __init__(self, world, rank, max_tokens, topk, F, D, E, device, group=None):
+    def __init__(self, world, rank, max_tokens, topk, F, FS, D, E, device, group=None):
         self.world, self.rank, self.max_tokens = world, rank, max_tokens
-        self.topk, self.F, self.D, self.E = topk, F, D, E
+        self.topk, self.F, self.FS, self.D, self.E = topk, F, FS, D, E
         self.device = torch.device(device)
         self.group = group
         ib, wb = ctypes.c_size_t(0), ctypes.c_size_t(0)
-        L.call("hsd_ep_buffer_bytes", world, max_tokens, topk, F, D, E, ctypes.byref(ib), ctypes.byref(wb))
+        L.call("hsd_ep_buffer_bytes", world, max_tokens, topk, F, FS, D, E, ctypes.byref(ib), ctypes.byref(wb))
         self.inbox_bytes, self.workspace_bytes = ib.value, wb.value
         with torch.cuda.device(self.device):
             p = ctypes.c_void_p(0)
@@ -213,7 +214,7 @@ class PeerInboxes:
             if world > 1:
                 handle = (ctypes.c_ubyte * 64)()
                 L.call("hsd_ep_ipc_handle", ctypes.c_void_p(self.inbox), ctypes.cast(handle, ctypes.c_void_p))
-                mine = (bytes(handle), (world, max_tokens, topk, F, D, E))
+                mine = (bytes(handle), (world, max_tokens, topk, F, FS, D, E))
                 everyone = [None] * world
                 dist.all_gather_object(everyone, mine, group=group)
                 for r, (h, cfg) in enumerate(everyone):
@@ -274,12 +275,14 @@ class ExpertParallelDown:
         self.pw, self.ps, self.pb = pw, ps, pb
         self.s_code = L.dtype_code(ps, "ExpertParallelDown scales")
         self.max_tokens = max_tokens
-        self.inboxes = inboxes or PeerInboxes(self.world, self.rank, max_tokens, topk, F, D, E, pw.device, group)
+        self.inboxes = inboxes or PeerInboxes(self.world, self.rank, max_tokens, topk, F, FS, D, E, pw.device, group)
         ib = self.inboxes
-        if (ib.world, ib.rank, ib.max_tokens, ib.topk, ib.F, ib.D, ib.E) != (self.world, self.rank, max_tokens, topk,
-                                                                         F, D, E):
+        if (ib.world, ib.rank, ib.max_tokens, ib.topk, ib.F, ib.FS, ib.D, ib.E) != (self.world, self.rank, max_tokens,
+                                                                                 topk, F, FS, D, E):
             raise ValueError("ExpertParallelDown: the inboxes were made for another configuration")
-        self.shared_down = _kernel_shared_down(spw, sps, spb, FS, D) if FS > 0 else None
+        if FS > 0 and (spw is None or sps is None or spb is None):
+            raise ValueError("ExpertParallelDown: FS > 0 needs the shared expert's spw, sps, spb")
+        self.spw, self.sps, self.spb = spw, sps, spb
         self.timeout_s = float(timeout_s)
         self.timing = timing
         self._events = None
@@ -293,15 +296,15 @@ class ExpertParallelDown:
 
     def phase_ms(self):
         """The last timed call's device time per phase (ms) on this rank: dispatch (routing and
-        the rows out), shared (this rank's shared expert), expert (waiting for the rows in, the
-        GEMM and the partial rows out), combine (waiting for the partials in and the sums)."""
+        the rows out), expert (waiting for the rows in, the one GEMM over the received rows and
+        this rank's shared expert, the partial rows out), combine (waiting for the partials in
+        and the sums)."""
         if self._events is None:
             return None
         self._events[-1].synchronize()
         e = self._events
-        return {"dispatch": e[0].elapsed_time(e[1]), "shared": e[1].elapsed_time(e[2]),
-                "expert": e[2].elapsed_time(e[3]), "combine": e[3].elapsed_time(e[4]),
-                "total": e[0].elapsed_time(e[4])}
+        return {"dispatch": e[0].elapsed_time(e[1]), "expert": e[1].elapsed_time(e[2]),
+                "combine": e[2].elapsed_time(e[3]), "total": e[0].elapsed_time(e[3])}
 
     def __call__(self, hcat, sel, gains):
         """hcat [B, topk*F + FS] bf16 / f16, sel [B, topk] int32 (global ids), gains [B, topk+1]
@@ -324,20 +327,18 @@ class ExpertParallelDown:
         ib = self.inboxes
         ws = L.ptr(ib.workspace)
         if self.timing:
-            self._events = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            self._events = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        hp = L.ptr(hcat) if B else None
         self._mark(0)
-        L.call("hsd_ep_dispatch", ws, self.rank, self.world, self.max_tokens, L.ptr(hcat), h_code, L.ptr(sel),
-               L.ptr(gains), B, K, F, self.FS, D, self.E, self.timeout_s, st)
+        L.call("hsd_ep_dispatch", ws, self.rank, self.world, self.max_tokens, hp, h_code, L.ptr(sel) if B else None,
+               L.ptr(gains) if B else None, B, K, F, self.FS, D, self.E, self.timeout_s, st)
         self._mark(1)
-        y_shared = None
-        if self.shared_down is not None and B > 0:
-            y_shared = self.shared_down(hcat[:, K * F:].contiguous(), gains[:, K:]).contiguous()
+        L.call("hsd_ep_expert", ws, ctypes.c_void_p(ib.inbox), self.rank, self.world, self.max_tokens, hp, h_code, B,
+               L.ptr(self.pw), L.ptr(self.ps), L.ptr(self.pb), L.ptr(self.spw), L.ptr(self.sps), L.ptr(self.spb),
+               self.s_code, K, F, self.FS, D, self.E, self.timeout_s, st)
         self._mark(2)
-        L.call("hsd_ep_expert", ws, ctypes.c_void_p(ib.inbox), self.rank, self.world, self.max_tokens, L.ptr(self.pw),
-               L.ptr(self.ps), L.ptr(self.pb), self.s_code, h_code, K, F, D, self.E, self.timeout_s, st)
-        self._mark(3)
         y = torch.empty((B, D), dtype=torch.float32, device=dev)
-        L.call("hsd_ep_combine", ws, self.rank, self.world, self.max_tokens, L.ptr(y_shared), L.ptr(y) if B else None,
-               B, K, F, D, self.E, self.timeout_s, st)
-        self._mark(4)
+        L.call("hsd_ep_combine", ws, self.rank, self.world, self.max_tokens, L.ptr(y) if B else None, B, K, F, self.FS,
+               D, self.E, self.timeout_s, st)
+        self._mark(3)
         return y

@@ -124,7 +124,7 @@ def test_ep_one_gpu_path_matches_operator(cuda, T):
     torch.cuda.synchronize()
     assert rel_err(y.cpu().numpy(), ref) < 5e-3
     assert rel_err(yc.cpu().numpy(), ref) < 5e-3
-    assert ph["total"] > 0 and set(ph) == {"dispatch", "shared", "expert", "combine", "total"}
+    assert ph["total"] > 0 and set(ph) == {"dispatch", "expert", "combine", "total"}
     assert set(coll.phase_ms()) == {"dispatch", "compute", "combine", "total"}
     assert hsd_b200.device_status() == 0
     ep.inboxes.close()
@@ -176,7 +176,7 @@ def test_ep_wait_for_a_missing_rank_times_out_with_status(cuda):
     E, F, FS, D, K = c["E"], c["F"], c["FS"], c["D"], c["topk"]
     assert hsd_b200.device_status() == 0
     ib, wb = ctypes.c_size_t(0), ctypes.c_size_t(0)
-    L.call("hsd_ep_buffer_bytes", 2, 8, K, F, D, E, ctypes.byref(ib), ctypes.byref(wb))
+    L.call("hsd_ep_buffer_bytes", 2, 8, K, F, FS, D, E, ctypes.byref(ib), ctypes.byref(wb))
     p = ctypes.c_void_p(0)
     L.call("hsd_ep_alloc", ib.value, ctypes.byref(p))
     try:
@@ -185,12 +185,13 @@ def test_ep_wait_for_a_missing_rank_times_out_with_status(cuda):
         st = L.stream_of(ws)
         L.call("hsd_ep_set_peers", L.ptr(ws), ctypes.cast(table, ctypes.c_void_p), 2, st)
         pw, ps, pb = (t[0::2].contiguous() for t in wts[:3])
+        spw, sps, spb = wts[3:]
         y = torch.empty((8, D), dtype=torch.float32, device=cuda)
         L.call("hsd_ep_dispatch", L.ptr(ws), 0, 2, 8, L.ptr(c["h"]), L.HSD_BF16, L.ptr(c["sel"]), L.ptr(c["gains"]),
                8, K, F, FS, D, E, 0.2, st)
-        L.call("hsd_ep_expert", L.ptr(ws), p, 0, 2, 8, L.ptr(pw), L.ptr(ps), L.ptr(pb), L.HSD_BF16, L.HSD_BF16, K, F, D,
-               E, 0.2, st)
-        L.call("hsd_ep_combine", L.ptr(ws), 0, 2, 8, None, L.ptr(y), 8, K, F, D, E, 0.2, st)
+        L.call("hsd_ep_expert", L.ptr(ws), p, 0, 2, 8, L.ptr(c["h"]), L.HSD_BF16, 8, L.ptr(pw), L.ptr(ps), L.ptr(pb),
+               L.ptr(spw), L.ptr(sps), L.ptr(spb), L.HSD_BF16, K, F, FS, D, E, 0.2, st)
+        L.call("hsd_ep_combine", L.ptr(ws), 0, 2, 8, L.ptr(y), 8, K, F, FS, D, E, 0.2, st)
         torch.cuda.synchronize()
         assert hsd_b200.device_status() == L.HSD_ERR_TIMEOUT
         assert hsd_b200.device_status() == 0                    # read and cleared
