@@ -446,6 +446,9 @@ def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512, dead_groups
                     "tiles incl. padding x every K-group (fp16 operands, fp32 accumulate)"}
 
 
+N_HOT_EXPERTS = 8      # experts replicated on every rank in the peer-memory EP leg (at > 1 GPU)
+
+
 def ep_leg(layers, device, dist_on, reps=10):
     """Expert-parallel MoE down projection across the ranks (layer 0's experts sharded round
     robin, E/G per GPU, tokens on their home rank): batch decode B = 64 and a prefill chunk of
@@ -459,7 +462,7 @@ def ep_leg(layers, device, dist_on, reps=10):
     phases of one call are timed with CUDA events on every rank.
     -> dict of tokens/s (device time, max over ranks), parity, phases."""
     hsd_b200 = _hsd()
-    from hsd_b200.ep import ExpertParallelDown, ExpertParallelDownCollective, shard_experts
+    from hsd_b200.ep import ExpertParallelDown, ExpertParallelDownCollective, hottest_experts, shard_experts
     if dist_on:
         import torch.distributed as dist
         world, rank = dist.get_world_size(), dist.get_rank()
@@ -467,7 +470,11 @@ def ep_leg(layers, device, dist_on, reps=10):
         world, rank = 1, 0
     pw, ps, pb, spw, sps, spb = layers[0]
     mine = shard_experts(pw, ps, pb, rank, world)
-    p2p = ExpertParallelDown(E, F, FS, D, TOPK, *mine, spw, sps, spb, max_tokens=512)
+    # the 8 most used experts of a calibration batch (all ranks' routing) go on every rank
+    calib, _ = synth.route_zipf(512, E, TOPK, torch.Generator(device=device).manual_seed(7 + rank), device)
+    hot = hottest_experts(calib, E, N_HOT_EXPERTS) if world > 1 else []
+    p2p = ExpertParallelDown(E, F, FS, D, TOPK, *shard_experts(pw, ps, pb, rank, world, replicated=hot), spw, sps, spb,
+                             max_tokens=512, replicated=hot)
     coll = ExpertParallelDownCollective(E, F, FS, D, TOPK, *mine, spw, sps, spb)
 
     def phases(ep, h, sel, gains):
@@ -528,8 +535,11 @@ def ep_leg(layers, device, dist_on, reps=10):
                                              "rel_err": v[2], "phases_ms_max_over_ranks": dict(zip(keys_c, v[7:11]))}}
     p2p.inboxes.close()
     out["gpus"] = world
+    out["replicated_experts"] = hot
     out["parity_ok"] = worst < 5e-3
-    out["note"] = ("experts placed round robin (e % G), E/G per GPU. ms / tokens_per_s: the peer-memory form "
+    out["note"] = ("experts placed round robin (e % G), E/G per GPU; in the peer-memory form the 8 most used experts "
+                   "of a calibration batch are also held by every rank (their slots computed at home; none at one "
+                   "GPU); the collective baseline is plain round robin. ms / tokens_per_s: the peer-memory form "
                    "(hsd_ep_dispatch / hsd_ep_expert / hsd_ep_combine: plain stores into the other GPUs' inboxes "
                    "over NVLink, release / acquire flags, no host read) replayed from a CUDA graph; eager_*: the "
                    "same calls launched from Python; collective_baseline: NCCL all_to_all_single exchanges around "

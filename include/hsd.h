@@ -349,9 +349,10 @@ int hsd_sparse_down_prefill_noalloc(const void* h, int h_dtype, const float* gai
 #define HSD_EP_IPC_HANDLE_BYTES 64
 
 /* Bytes of a rank's inbox and of its private workspace (256-byte aligned, from any
- * allocator). At world 8, max_tokens 512 and the reference shapes: 130 MB and 203 MB. */
+ * allocator). n_local: the routed experts the rank holds (<= 0: E / world); the inbox does
+ * not depend on it. At world 8, max_tokens 512 and the reference shapes: 130 MB and 203 MB. */
 int hsd_ep_buffer_bytes(int world, int max_tokens, int topk, int F, int FS, int D, int E,
-                        size_t* inbox_bytes, size_t* workspace_bytes);
+                        int n_local, size_t* inbox_bytes, size_t* workspace_bytes);
 /* Zeroed device memory that other processes can map (cudaMalloc; free with hsd_ep_free).
  * The one allocation this library makes, and only here. */
 int hsd_ep_alloc(size_t bytes, void** ptr);
@@ -366,20 +367,25 @@ int hsd_ep_ipc_close(void* ptr);
 int hsd_ep_set_peers(void* workspace, const uint64_t* inbox_addrs, int world, void* stream);
 /* Routes this rank's B tokens: hcat [B, topk*F + FS] (bf16 or f16, 16-byte aligned), sel
  * [B, topk] int32 global expert ids, gains [B, topk+1] f32. Each (token, slot) row goes to its
- * expert's owner with its local id and gain. An id outside [0, E) is recorded as
- * HSD_ERR_INDEX and the slot contributes nothing defined. */
+ * expert's owner with its local id and gain. emap (device, [E] int32, this rank's table, or
+ * NULL for round robin: owner e % world, local id e / world): emap[e] = owner << 16 | local id
+ * at the owner; an expert replicated on every rank maps to this rank itself. An id outside
+ * [0, E), or a table entry naming no rank, is recorded as HSD_ERR_INDEX and the slot
+ * contributes nothing defined. */
 int hsd_ep_dispatch(void* workspace, int rank, int world, int max_tokens, const void* hcat,
                     int h_dtype, const int32_t* sel, const float* gains, int B, int topk, int F,
-                    int FS, int D, int E, double timeout_s, void* stream);
-/* The GEMM side: the slots this rank received times its experts pw [E/world, F, D/8], ps / pb
- * [E/world, F/64, D] (neuron-major, s_dtype bf16 or f16, owned_experts order), and the shared
+                    int FS, int D, int E, const int32_t* emap, double timeout_s, void* stream);
+/* The GEMM side: the slots this rank received times its n_local experts pw [n_local, F, D/8],
+ * ps / pb [n_local, F/64, D] (neuron-major, s_dtype bf16 or f16, local-id order; n_local <= 0:
+ * E / world), and the shared
  * expert spw [FS, D/8], sps / spb [FS/64, D] of this rank's own B tokens (the same hcat as the
  * dispatch), in one tensor-core GEMM launch; each fp32 partial row times its gain is stored
  * into its home rank's inbox. inbox: this rank's own inbox. */
 int hsd_ep_expert(void* workspace, void* inbox, int rank, int world, int max_tokens,
                   const void* hcat, int h_dtype, int B, const uint32_t* pw, const void* ps,
                   const void* pb, const uint32_t* spw, const void* sps, const void* spb,
-                  int s_dtype, int topk, int F, int FS, int D, int E, double timeout_s, void* stream);
+                  int s_dtype, int topk, int F, int FS, int D, int E, int n_local, double timeout_s,
+                  void* stream);
 /* y [B, D] f32 = the sum over each token's topk partial rows in slot order, then its shared
  * expert row (FS > 0). */
 int hsd_ep_combine(void* workspace, int rank, int world, int max_tokens, float* y, int B,

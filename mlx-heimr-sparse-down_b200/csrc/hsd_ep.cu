@@ -1,8 +1,10 @@
 // Expert parallelism over the GPUs of one box (a multi-GPU form of hsd/decode.py's sparse_down
 // and hsd/prefill.py's sparse_down_prefill; the reference runs on one Apple GPU).
 //
-// Routed expert e lives on rank e % G (round robin), the shared expert is replicated, tokens
-// stay on their home rank. Every rank owns an INBOX: device memory allocated with
+// Routed expert e lives on rank e % G (round robin) unless a placement table says otherwise
+// (emap[e] = owner << 16 | local id; hot experts replicated on every rank map to the home rank
+// itself, so their slots never leave it), the shared expert is replicated, tokens stay on their
+// home rank. Every rank owns an INBOX: device memory allocated with
 // hsd_ep_alloc, mapped into every other rank's process (CUDA IPC), which the other ranks write
 // with plain stores over NVLink -- no collective library, no multicast, no host round trip:
 //
@@ -71,7 +73,9 @@ struct EpLayout {
   size_t w_peers, w_misc, w_pos, w_te, w_ts, w_km, w_hc, w_rowdst, ws_bytes;
 };
 
-int ep_layout(int world, int max_tokens, int topk, int F, int FS, int D, int E, EpLayout* L) {
+// n_local: the routed experts this rank holds (<= 0: E / world, the round-robin share); only
+// the private workspace depends on it, the inbox layout is the same on every rank.
+int ep_layout(int world, int max_tokens, int topk, int F, int FS, int D, int E, int n_local, EpLayout* L) {
   if (world < 1 || world > kMaxWorld)
     return hsd::set_error(HSD_ERR_SHAPE, "ep: world %d outside 1..%d", world, kMaxWorld);
   if (max_tokens < 1 || topk < 1 || F < 64 || F % 64 != 0 || FS < 0 || FS % 64 != 0 || D < 192 || D % 192 != 0 ||
@@ -83,7 +87,8 @@ int ep_layout(int world, int max_tokens, int topk, int F, int FS, int D, int E, 
   const long long S = static_cast<long long>(max_tokens) * topk;
   if (S >= (1ll << 24) || S * world >= (1ll << 27))
     return hsd::set_error(HSD_ERR_SHAPE, "ep: max_tokens * topk * world too large (%lld slots)", S * world);
-  if (E / world > 256) return hsd::set_error(HSD_ERR_SHAPE, "ep: more than 256 experts per rank");
+  if (n_local <= 0) n_local = E / world;
+  if (n_local > 256 || n_local > E) return hsd::set_error(HSD_ERR_SHAPE, "ep: %d local experts (at most 256 and E)", n_local);
   L->G = world;
   L->S = static_cast<int>(S);
   L->R = static_cast<int>(S * world);
@@ -91,7 +96,7 @@ int ep_layout(int world, int max_tokens, int topk, int F, int FS, int D, int E, 
   L->F = F;
   L->FS = FS;
   L->D = D;
-  L->E_local = E / world;
+  L->E_local = n_local;
   int nr = 0, ns = 0;
   int rc = hsd::prefill_tile_counts(L->R, 1, L->E_local, hsd::kPrefillTile, &nr, &ns);
   if (rc) return rc;
@@ -163,6 +168,7 @@ struct InboxOffsets {
 //      written into every rank's inbox, then published with the epoch.
 __global__ void __launch_bounds__(kRouteThreads) ep_route_kernel(const uint64_t* __restrict__ peers, int rank, int G,
                                                                  const int32_t* __restrict__ sel, int nslots, int E,
+                                                                 const int32_t* __restrict__ emap,
                                                                  int32_t* __restrict__ pos) {
   __shared__ int running[kMaxWorld];
   __shared__ int tab[kRouteThreads / 32][kMaxWorld];
@@ -176,8 +182,9 @@ __global__ void __launch_bounds__(kRouteThreads) ep_route_kernel(const uint64_t*
     int d = -1;
     if (j < nslots) {
       const int e = sel[j];
-      if (e >= 0 && e < E) {
-        d = e % G;
+      const int o = (e >= 0 && e < E) ? (emap ? (emap[e] >> 16) : e % G) : -1;
+      if (o >= 0 && o < G) {
+        d = o;
       } else {
         hsd_flag_ep(HSD_ERR_INDEX);   // kept home without an expert: the owner drops it
         d = rank;
@@ -226,7 +233,8 @@ __global__ void __launch_bounds__(kScatterThreads) ep_scatter_kernel(const uint6
                                                                      const int32_t* __restrict__ sel,
                                                                      const float* __restrict__ gains,
                                                                      const int32_t* __restrict__ pos, int nslots,
-                                                                     int topk, int F, int FS, int E, InboxOffsets off,
+                                                                     int topk, int F, int FS, int E,
+                                                                     const int32_t* __restrict__ emap, InboxOffsets off,
                                                                      unsigned long long timeout_ns) {
   const int NR = topk * F + FS;
   __shared__ int base[kMaxWorld];
@@ -261,7 +269,7 @@ __global__ void __launch_bounds__(kScatterThreads) ep_scatter_kernel(const uint6
       for (int i = lane; i < row_bytes / 16; i += 32) dh[i] = hsd::ldg_nc_v4(src + i);
       if (lane == 0) {
         const int e = sel[j];
-        reinterpret_cast<int32_t*>(dst + off.sel_in)[row] = (e >= 0 && e < E) ? e / G : -1;
+        reinterpret_cast<int32_t*>(dst + off.sel_in)[row] = (e >= 0 && e < E) ? (emap ? (emap[e] & 0xFFFF) : e / G) : -1;
         reinterpret_cast<float*>(dst + off.g_in)[2 * static_cast<int64_t>(row)] =
             gains[static_cast<int64_t>(b) * (topk + 1) + k];
         reinterpret_cast<int32_t*>(dst + off.ret_in)[row] = rank * S + j;
@@ -386,11 +394,11 @@ int check_rank(int rank, int world, const void* ws) {
 
 // ---- C ABI -------------------------------------------------------------------------------
 
-extern "C" int hsd_ep_buffer_bytes(int world, int max_tokens, int topk, int F, int FS, int D, int E,
+extern "C" int hsd_ep_buffer_bytes(int world, int max_tokens, int topk, int F, int FS, int D, int E, int n_local,
                                    size_t* inbox_bytes, size_t* workspace_bytes) {
   if (!inbox_bytes || !workspace_bytes) return hsd::set_error(HSD_ERR_ARG, "hsd_ep_buffer_bytes: null output");
   EpLayout L;
-  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, &L);
+  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, n_local, &L);
   if (rc) return rc;
   *inbox_bytes = L.inbox_bytes;
   *workspace_bytes = L.ws_bytes;
@@ -455,9 +463,9 @@ extern "C" int hsd_ep_set_peers(void* workspace, const uint64_t* inbox_addrs, in
 
 extern "C" int hsd_ep_dispatch(void* workspace, int rank, int world, int max_tokens, const void* hcat, int h_dtype,
                                const int32_t* sel, const float* gains, int B, int topk, int F, int FS, int D, int E,
-                               double timeout_s, void* stream) {
+                               const int32_t* emap, double timeout_s, void* stream) {
   EpLayout L;
-  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, &L);
+  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, 0, &L);
   if (rc) return rc;
   if ((rc = check_rank(rank, world, workspace))) return rc;
   if (B < 0 || B > max_tokens)
@@ -470,11 +478,11 @@ extern "C" int hsd_ep_dispatch(void* workspace, int rank, int world, int max_tok
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   const uint64_t* peers = reinterpret_cast<const uint64_t*>(ws + L.w_peers);
   int32_t* pos = reinterpret_cast<int32_t*>(ws + L.w_pos);
-  ep_route_kernel<<<1, kRouteThreads, 0, st>>>(peers, rank, world, sel, B * topk, E, pos);
+  ep_route_kernel<<<1, kRouteThreads, 0, st>>>(peers, rank, world, sel, B * topk, E, emap, pos);
   if ((rc = hsd::check_launch("hsd_ep_dispatch: route"))) return rc;
   ep_scatter_kernel<<<kScatterCTAs, kScatterThreads, 0, st>>>(peers, rank, world, L.S,
                                                               static_cast<const unsigned char*>(hcat), sel, gains, pos,
-                                                              B * topk, topk, F, FS, E, offsets_of(L),
+                                                              B * topk, topk, F, FS, E, emap, offsets_of(L),
                                                               timeout_ns_of(timeout_s));
   return hsd::check_launch("hsd_ep_dispatch: scatter");
 }
@@ -482,9 +490,9 @@ extern "C" int hsd_ep_dispatch(void* workspace, int rank, int world, int max_tok
 extern "C" int hsd_ep_expert(void* workspace, void* inbox_ptr, int rank, int world, int max_tokens, const void* hcat,
                              int h_dtype, int B, const uint32_t* pw, const void* ps, const void* pb,
                              const uint32_t* spw, const void* sps, const void* spb, int s_dtype, int topk, int F, int FS,
-                             int D, int E, double timeout_s, void* stream) {
+                             int D, int E, int n_local, double timeout_s, void* stream) {
   EpLayout L;
-  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, &L);
+  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, n_local, &L);
   if (rc) return rc;
   if ((rc = check_rank(rank, world, workspace))) return rc;
   if (B < 0 || B > max_tokens)
@@ -532,7 +540,7 @@ extern "C" int hsd_ep_expert(void* workspace, void* inbox_ptr, int rank, int wor
 extern "C" int hsd_ep_combine(void* workspace, int rank, int world, int max_tokens, float* y, int B, int topk, int F,
                               int FS, int D, int E, double timeout_s, void* stream) {
   EpLayout L;
-  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, &L);
+  int rc = ep_layout(world, max_tokens, topk, F, FS, D, E, 0, &L);
   if (rc) return rc;
   if ((rc = check_rank(rank, world, workspace))) return rc;
   if (B < 0 || B > max_tokens)

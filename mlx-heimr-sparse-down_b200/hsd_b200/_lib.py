@@ -60,15 +60,15 @@ SIGNATURES = {
     "hsd_prefill_noalloc_max_bytes": [_P],
     "hsd_sparse_down_prefill_noalloc": [_P, _I, _P, _P, _P, _I, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I,
                                         _I, _I, _I, _I, _I, _I, _P],
-    "hsd_ep_buffer_bytes": [_I, _I, _I, _I, _I, _I, _I, _P, _P],
+    "hsd_ep_buffer_bytes": [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P],
     "hsd_ep_alloc": [ctypes.c_size_t, _P],
     "hsd_ep_free": [_P],
     "hsd_ep_ipc_handle": [_P, _P],
     "hsd_ep_ipc_open": [_P, _P],
     "hsd_ep_ipc_close": [_P],
     "hsd_ep_set_peers": [_P, _P, _I, _P],
-    "hsd_ep_dispatch": [_P, _I, _I, _I, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, ctypes.c_double, _P],
-    "hsd_ep_expert": [_P, _P, _I, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I,
+    "hsd_ep_dispatch": [_P, _I, _I, _I, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _P, ctypes.c_double, _P],
+    "hsd_ep_expert": [_P, _P, _I, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
                       ctypes.c_double, _P],
     "hsd_ep_combine": [_P, _I, _I, _I, _P, _I, _I, _I, _I, _I, _I, ctypes.c_double, _P],
 }

@@ -47,9 +47,50 @@ def owned_experts(E, rank, world):
     return list(range(rank, E, world))
 
 
-def shard_experts(pw, ps, pb, rank, world):
-    """This rank's slice of a full neuron-major expert stack ([E, ...] each), contiguous."""
-    return tuple(t[rank::world].contiguous() for t in (pw, ps, pb))
+def expert_placement(E, world, replicated=()):
+    """Where every routed expert lives. Expert e belongs to rank e % world (round robin) unless it
+    is in `replicated`, a list of hot experts held by EVERY rank: a slot routed to one of those is
+    computed on its own home rank and never crosses NVLink (under the benchmark's Zipf(1.1)
+    routing, replicating the 8 most used experts cuts the busiest rank's slots from 1.70x to
+    1.09x the mean at 8 GPUs, for 8 more expert stacks per rank). Rank r's local experts are its
+    owned ones in ascending id, then the replicated ones in the given order.
+    -> (local: per rank the global ids in local-id order, emap: per rank a list of E ints,
+    owner << 16 | local id at the owner, replicated experts mapped to the rank itself)."""
+    rep = list(dict.fromkeys(int(e) for e in replicated))
+    if any(not 0 <= e < E for e in rep):
+        raise ValueError(f"expert_placement: replicated ids must be in [0, {E})")
+    repset = set(rep)
+    owned = [[e for e in range(E) if e % world == r and e not in repset] for r in range(world)]
+    where = {e: (r, i) for r in range(world) for i, e in enumerate(owned[r])}
+    local = [owned[r] + rep for r in range(world)]
+    emap = []
+    for r in range(world):
+        m = []
+        for e in range(E):
+            if e in repset:
+                m.append((r << 16) | (len(owned[r]) + rep.index(e)))
+            else:
+                o, i = where[e]
+                m.append((o << 16) | i)
+        emap.append(m)
+    return local, emap
+
+
+def hottest_experts(sel, E, n, group=None):
+    """The n experts with the most slots in `sel` (summed over the ranks of `group` when a process
+    group is up): a one-time calibration for `replicated`."""
+    cnt = torch.bincount(sel.reshape(-1).long(), minlength=E).to(torch.float64)
+    if dist.is_available() and dist.is_initialized():
+        dist.all_reduce(cnt, group=group)
+    return [int(e) for e in torch.argsort(cnt, descending=True, stable=True)[:n].tolist()]
+
+
+def shard_experts(pw, ps, pb, rank, world, replicated=()):
+    """This rank's stack of a full neuron-major expert stack ([E, ...] each), in local-id order
+    (expert_placement), contiguous."""
+    ids = expert_placement(pw.shape[0], world, replicated)[0][rank]
+    idx = torch.tensor(ids, dtype=torch.long, device=pw.device)
+    return tuple(t.index_select(0, idx).contiguous() for t in (pw, ps, pb))
 
 
 def _kernel_local_down(pw, ps, pb, F, D, E_local):
@@ -195,13 +236,15 @@ class PeerInboxes:
     synchronises the device, waits for every rank, unmaps the peers' inboxes and frees this
     rank's; without it the memory stays until the process exits."""
 
-    def __init__(self, world, rank, max_tokens, topk, F, FS, D, E, device, group=None):
+    def __init__(self, world, rank, max_tokens, topk, F, FS, D, E, device, group=None, n_local=0):
         self.world, self.rank, self.max_tokens = world, rank, max_tokens
         self.topk, self.F, self.FS, self.D, self.E = topk, F, FS, D, E
+        self.n_local = n_local if n_local > 0 else E // world
         self.device = torch.device(device)
         self.group = group
         ib, wb = ctypes.c_size_t(0), ctypes.c_size_t(0)
-        L.call("hsd_ep_buffer_bytes", world, max_tokens, topk, F, FS, D, E, ctypes.byref(ib), ctypes.byref(wb))
+        L.call("hsd_ep_buffer_bytes", world, max_tokens, topk, F, FS, D, E, self.n_local, ctypes.byref(ib),
+               ctypes.byref(wb))
         self.inbox_bytes, self.workspace_bytes = ib.value, wb.value
         with torch.cuda.device(self.device):
             p = ctypes.c_void_p(0)
@@ -253,14 +296,16 @@ class ExpertParallelDown:
 
     pw / ps / pb: this rank's experts (owned_experts order) [E/G, F, D/8] / [E/G, F/64, D]
     (neuron-major; shard_experts slices a full stack); spw / sps / spb: the shared expert
-    (replicated). max_tokens bounds B per call (it sizes the inbox); inboxes: a PeerInboxes to
-    share between layers (else one is made, collectively). Without an initialised process group
+    (replicated). replicated: hot expert ids every rank holds (expert_placement; pw / ps / pb then
+    hold this rank's owned experts followed by those, as shard_experts(..., replicated) gives).
+    max_tokens bounds B per call (it sizes the inbox); inboxes: a PeerInboxes to share between
+    layers with the same placement (else one is made, collectively). Without an initialised process group
     the object runs alone (world size 1) on its own inbox. timing=True records CUDA events
     around the phases of every call; phase_ms() reads the last call's. Every rank must make
     the same calls in the same order (B may differ, and may be 0)."""
 
     def __init__(self, E, F, FS, D, topk, pw, ps, pb, spw=None, sps=None, spb=None, group=None, max_tokens=512,
-                 inboxes=None, timeout_s=10.0, timing=False):
+                 inboxes=None, timeout_s=10.0, timing=False, replicated=()):
         self.group = group
         self.distributed = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(group) if self.distributed else 1
@@ -268,17 +313,21 @@ class ExpertParallelDown:
         if E % self.world:
             raise ValueError(f"ExpertParallelDown: E={E} is not divisible by {self.world} ranks")
         self.E, self.F, self.FS, self.D, self.topk = E, F, FS, D, topk
-        self.E_local = E // self.world
+        local, emap = expert_placement(E, self.world, replicated)
+        self.local_ids = local[self.rank]
+        self.E_local = len(self.local_ids)
         L.require_cuda(pw, ps, pb, spw, sps, spb, what="ExpertParallelDown")
         if pw.shape[0] != self.E_local:
             raise ValueError(f"ExpertParallelDown: {pw.shape[0]} local experts given, {self.E_local} expected")
+        self.emap = (torch.tensor(emap[self.rank], dtype=torch.int32, device=pw.device) if len(replicated) else None)
         self.pw, self.ps, self.pb = pw, ps, pb
         self.s_code = L.dtype_code(ps, "ExpertParallelDown scales")
         self.max_tokens = max_tokens
-        self.inboxes = inboxes or PeerInboxes(self.world, self.rank, max_tokens, topk, F, FS, D, E, pw.device, group)
+        self.inboxes = inboxes or PeerInboxes(self.world, self.rank, max_tokens, topk, F, FS, D, E, pw.device, group,
+                                              n_local=self.E_local)
         ib = self.inboxes
-        if (ib.world, ib.rank, ib.max_tokens, ib.topk, ib.F, ib.FS, ib.D, ib.E) != (self.world, self.rank, max_tokens,
-                                                                                 topk, F, FS, D, E):
+        if (ib.world, ib.rank, ib.max_tokens, ib.topk, ib.F, ib.FS, ib.D, ib.E, ib.n_local) != (
+                self.world, self.rank, max_tokens, topk, F, FS, D, E, self.E_local):
             raise ValueError("ExpertParallelDown: the inboxes were made for another configuration")
         if FS > 0 and (spw is None or sps is None or spb is None):
             raise ValueError("ExpertParallelDown: FS > 0 needs the shared expert's spw, sps, spb")
@@ -331,11 +380,11 @@ class ExpertParallelDown:
         hp = L.ptr(hcat) if B else None
         self._mark(0)
         L.call("hsd_ep_dispatch", ws, self.rank, self.world, self.max_tokens, hp, h_code, L.ptr(sel) if B else None,
-               L.ptr(gains) if B else None, B, K, F, self.FS, D, self.E, self.timeout_s, st)
+               L.ptr(gains) if B else None, B, K, F, self.FS, D, self.E, L.ptr(self.emap), self.timeout_s, st)
         self._mark(1)
         L.call("hsd_ep_expert", ws, ctypes.c_void_p(ib.inbox), self.rank, self.world, self.max_tokens, hp, h_code, B,
                L.ptr(self.pw), L.ptr(self.ps), L.ptr(self.pb), L.ptr(self.spw), L.ptr(self.sps), L.ptr(self.spb),
-               self.s_code, K, F, self.FS, D, self.E, self.timeout_s, st)
+               self.s_code, K, F, self.FS, D, self.E, self.E_local, self.timeout_s, st)
         self._mark(2)
         y = torch.empty((B, D), dtype=torch.float32, device=dev)
         L.call("hsd_ep_combine", ws, self.rank, self.world, self.max_tokens, L.ptr(y) if B else None, B, K, F, self.FS,

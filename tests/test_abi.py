@@ -89,28 +89,30 @@ def test_python_wrappers_refuse_cpu_tensors():
 
 def test_ep_buffer_sizes_and_argument_checks():
     ib, wb = ctypes.c_size_t(0), ctypes.c_size_t(0)
-    assert _rc("hsd_ep_buffer_bytes", 8, 512, 6, 1856, 3712, 2688, 128, ctypes.byref(ib), ctypes.byref(wb)) == L.HSD_OK
+    assert _rc("hsd_ep_buffer_bytes", 8, 512, 6, 1856, 3712, 2688, 128, 0, ctypes.byref(ib), ctypes.byref(wb)) == L.HSD_OK
     # inbox: 8 ranks x 3072 slots of h rows + ids, gains, return addresses, + 3072 + 512 fp32 partial rows
     assert 130e6 < ib.value < 131e6
     assert 202e6 < wb.value < 204e6         # dominated by the gathered fp16 A tiles (K up to FS)
     one_i, one_w = ctypes.c_size_t(0), ctypes.c_size_t(0)
-    assert _rc("hsd_ep_buffer_bytes", 1, 512, 6, 1856, 3712, 2688, 128, ctypes.byref(one_i), ctypes.byref(one_w)) == 0
+    assert _rc("hsd_ep_buffer_bytes", 1, 512, 6, 1856, 3712, 2688, 128, 0, ctypes.byref(one_i), ctypes.byref(one_w)) == 0
     assert one_i.value < ib.value
-    assert _rc("hsd_ep_buffer_bytes", 3, 512, 6, 1856, 3712, 2688, 128, ctypes.byref(ib), ctypes.byref(wb)) == L.HSD_ERR_SHAPE
-    assert _rc("hsd_ep_buffer_bytes", 17, 512, 6, 1856, 3712, 2688, 128, ctypes.byref(ib), ctypes.byref(wb)) == L.HSD_ERR_SHAPE
-    assert _rc("hsd_ep_buffer_bytes", 8, 512, 6, 1856, 3712, 2680, 128, ctypes.byref(ib), ctypes.byref(wb)) == L.HSD_ERR_SHAPE
+    assert _rc("hsd_ep_buffer_bytes", 3, 512, 6, 1856, 3712, 2688, 128, 0, ctypes.byref(ib), ctypes.byref(wb)) == L.HSD_ERR_SHAPE
+    assert _rc("hsd_ep_buffer_bytes", 17, 512, 6, 1856, 3712, 2688, 128, 0, ctypes.byref(ib), ctypes.byref(wb)) == L.HSD_ERR_SHAPE
+    assert _rc("hsd_ep_buffer_bytes", 8, 512, 6, 1856, 3712, 2680, 128, 0, ctypes.byref(ib), ctypes.byref(wb)) == L.HSD_ERR_SHAPE
     ws = ctypes.c_void_p(1 << 20)
     p = ctypes.c_void_p(256)
     d = lambda rank, B, ws=ws, h=L.HSD_BF16: _rc("hsd_ep_dispatch", ws, rank, 8, 512, p, h, p, p, B, 6, 1856,  # noqa: E731
-                                                 3712, 2688, 128, 1.0, None)
+                                                 3712, 2688, 128, None, 1.0, None)
     assert d(8, 4) == L.HSD_ERR_ARG             # rank outside the world
     assert d(0, 513) == L.HSD_ERR_SHAPE         # more tokens than max_tokens
     assert d(0, 4, ws=ctypes.c_void_p((1 << 20) + 16)) == L.HSD_ERR_ALIGN
     assert d(0, 4, h=L.HSD_F32) == L.HSD_ERR_DTYPE
     assert _rc("hsd_ep_expert", ws, None, 0, 8, 512, p, L.HSD_BF16, 4, p, p, p, p, p, p, L.HSD_BF16, 6, 1856, 3712,
-               2688, 128, 1.0, None) == L.HSD_ERR_ARG            # no inbox
+               2688, 128, 0, 1.0, None) == L.HSD_ERR_ARG            # no inbox
     assert _rc("hsd_ep_expert", ws, p, 0, 8, 512, p, L.HSD_BF16, 4, p, p, p, None, p, p, L.HSD_BF16, 6, 1856, 3712,
-               2688, 128, 1.0, None) == L.HSD_ERR_ARG            # no shared weights with FS > 0
+               2688, 128, 0, 1.0, None) == L.HSD_ERR_ARG            # no shared weights with FS > 0
+    assert _rc("hsd_ep_expert", ws, p, 0, 8, 512, p, L.HSD_BF16, 4, p, p, p, p, p, p, L.HSD_BF16, 6, 1856, 3712,
+               2688, 128, 300, 1.0, None) == L.HSD_ERR_SHAPE          # more than 256 local experts
     assert _rc("hsd_ep_combine", ws, 0, 8, 512, None, 4, 6, 1856, 3712, 2688, 128, 1.0, None) == L.HSD_ERR_ARG
     assert _rc("hsd_ep_set_peers", ws, None, 2, None) == L.HSD_ERR_ARG
     assert _rc("hsd_ep_alloc", 0, ctypes.byref(ctypes.c_void_p())) == L.HSD_ERR_ARG

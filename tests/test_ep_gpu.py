@@ -49,7 +49,7 @@ def _worker(rank, port, q):
         from hsd_b200 import synth
         from hsd_b200.ep import ExpertParallelDown, ExpertParallelDownCollective, shard_experts
         out = []
-        inboxes = None
+        inboxes = rep_inboxes = None
         for T in (8, 512):                  # batch decode rows, a prefill chunk, per rank
             c = synth.decode_case(seed=5, B=T * WORLD, zero_frac=0.9, device=dev, routing="zipf")
             pw, ps, pb = hsd_b200.to_neuron_major(c["w"], c["s"], c["b"])
@@ -66,11 +66,20 @@ def _worker(rank, port, q):
             ys = [p2p(*x) for _ in range(3)]     # three calls: epochs advance, buffers reused
             coll = ExpertParallelDownCollective(c["E"], c["F"], c["FS"], c["D"], c["topk"], *mine, spw, sps, spb)
             yc = coll(*x)
+            # hot experts on every rank: their slots stay home (placement table in the dispatch)
+            hot = [0, 1, 2, 5]
+            rep = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"],
+                                     *shard_experts(pw, ps, pb, rank, WORLD, replicated=hot), spw, sps, spb,
+                                     max_tokens=512, replicated=hot, inboxes=rep_inboxes)
+            rep_inboxes = rep.inboxes
+            yr = rep(*x)
             torch.cuda.synchronize()
             r = ref.cpu().numpy()
-            out.append((T, [rel_err(y.cpu().numpy(), r) for y in ys], rel_err(yc.cpu().numpy(), r),
-                        all(torch.equal(ys[0], y) for y in ys), hsd_b200.device_status()))
+            out.append((T, [rel_err(y.cpu().numpy(), r) for y in ys] + [rel_err(yr.cpu().numpy(), r)],
+                        rel_err(yc.cpu().numpy(), r), all(torch.equal(ys[0], y) for y in ys),
+                        hsd_b200.device_status()))
         inboxes.close()
+        rep_inboxes.close()
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -131,6 +140,27 @@ def test_ep_one_gpu_path_matches_operator(cuda, T):
 
 
 @pytest.mark.gpu
+def test_ep_placement_table_with_replicated_experts(cuda):
+    """A placement with replicated experts at world size 1: the local stack is the owned experts
+    then the replicated ones (a permutation of all 128), reached through the dispatch's table;
+    the output is the single-GPU operator's."""
+    import hsd_b200
+    from hsd_b200.ep import ExpertParallelDown, hottest_experts, shard_experts
+    T = 256
+    c, wts = _case(cuda, T, seed=11)
+    hot = hottest_experts(c["sel"], c["E"], 8)
+    assert hot[0] == 0                        # Zipf routing: expert 0 is the most used
+    ref = _single(hsd_b200, c, 0, T, *wts).cpu().numpy()
+    ep = ExpertParallelDown(c["E"], c["F"], c["FS"], c["D"], c["topk"], *shard_experts(*wts[:3], 0, 1, replicated=hot),
+                            *wts[3:], max_tokens=T, replicated=hot)
+    y = ep(c["h"], c["sel"], c["gains"])
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), ref) < 5e-3
+    assert hsd_b200.device_status() == 0
+    ep.inboxes.close()
+
+
+@pytest.mark.gpu
 def test_ep_call_replays_from_a_cuda_graph(cuda):
     """The peer-memory call reads nothing back to the host, so it captures: replays of the graph
     (each a new epoch of the flags) reproduce the eager call's bits on new inputs copied in."""
@@ -176,7 +206,7 @@ def test_ep_wait_for_a_missing_rank_times_out_with_status(cuda):
     E, F, FS, D, K = c["E"], c["F"], c["FS"], c["D"], c["topk"]
     assert hsd_b200.device_status() == 0
     ib, wb = ctypes.c_size_t(0), ctypes.c_size_t(0)
-    L.call("hsd_ep_buffer_bytes", 2, 8, K, F, FS, D, E, ctypes.byref(ib), ctypes.byref(wb))
+    L.call("hsd_ep_buffer_bytes", 2, 8, K, F, FS, D, E, 0, ctypes.byref(ib), ctypes.byref(wb))
     p = ctypes.c_void_p(0)
     L.call("hsd_ep_alloc", ib.value, ctypes.byref(p))
     try:
@@ -188,9 +218,9 @@ def test_ep_wait_for_a_missing_rank_times_out_with_status(cuda):
         spw, sps, spb = wts[3:]
         y = torch.empty((8, D), dtype=torch.float32, device=cuda)
         L.call("hsd_ep_dispatch", L.ptr(ws), 0, 2, 8, L.ptr(c["h"]), L.HSD_BF16, L.ptr(c["sel"]), L.ptr(c["gains"]),
-               8, K, F, FS, D, E, 0.2, st)
+               8, K, F, FS, D, E, None, 0.2, st)
         L.call("hsd_ep_expert", L.ptr(ws), p, 0, 2, 8, L.ptr(c["h"]), L.HSD_BF16, 8, L.ptr(pw), L.ptr(ps), L.ptr(pb),
-               L.ptr(spw), L.ptr(sps), L.ptr(spb), L.HSD_BF16, K, F, FS, D, E, 0.2, st)
+               L.ptr(spw), L.ptr(sps), L.ptr(spb), L.HSD_BF16, K, F, FS, D, E, 0, 0.2, st)
         L.call("hsd_ep_combine", L.ptr(ws), 0, 2, 8, L.ptr(y), 8, K, F, FS, D, E, 0.2, st)
         torch.cuda.synchronize()
         assert hsd_b200.device_status() == L.HSD_ERR_TIMEOUT
