@@ -15,21 +15,23 @@
 //   shared memory in a fixed rank order: deterministic, with no scratch memory, atomics or
 //   second kernel.
 //
-// Per CTA: 16 group lanes, lane L folding the CTA's groups L, L+16, L+32, ... in ascending
-// order into its own 8 outputs per word; a warp runs one or two group lanes (16 or 8 warps),
-// lane w of the warp owning word w of the chunk. Per round a warp takes two groups per group
-// lane and, with no shared-memory staging:
-//   1. loads the groups' h values (two per lane, one coalesced load per group), expert ids
-//      and gains, and builds each group's live mask with two ballots;
-//   2. starts, for every live group, the 16-byte cp.async copies of its scale and bias
-//      chunks into the warp's own shared-memory area, and loads the first RG live rows of
-//      every group straight into registers -- one coalesced 4-byte load per lane and row, all
-//      of them issued before any is used, so a round costs one memory round trip whatever
-//      the number of rows (a group with more than RG live rows takes further round trips);
-//   3. accumulates acc'[n] = sum h * (1 + q_n/16) and hsum = sum h over each group's live
-//      rows in ascending order (1 + q/16 built exactly from the nibble with bit operations,
-//      packed fp32 FMAs), and folds the group in as out[n] += g * (16*s[n]*(acc'[n] - hsum)
-//      + b[n]*hsum) -- the reference's affine algebra s * sum(h q) + b * sum(h).
+// Per CTA: 16 group lanes (one warp each), lane L folding the CTA's groups L, L+16, L+32, ...
+// in ascending order into its own 8 outputs per word, lane w of the warp owning word w of the
+// chunk. A round covers 32 groups, two per warp:
+//   1. the round's h values go to shared memory (16-byte cp.async pieces spread over the
+//      CTA's threads) while one warp reads the groups' expert ids and gains -- one memory
+//      round trip;
+//   2. each warp builds its two groups' live masks (two ballots each), compacts the live rows
+//      into a list (row, raw h) in shared memory, starts the cp.async copies of the first RG
+//      live rows' chunks (8 lanes a row, 16 bytes a lane, four rows per instruction: the
+//      memory system charges per request, not per byte), then the TMA bulk copies of the
+//      live groups' scale / bias chunks on the warp's mbarrier -- one more round trip (a group
+//      with more than RG live rows takes further ones);
+//   3. each group's staged words and h values are read into registers, then its rows are
+//      accumulated in ascending order: acc[n] += h * (8 + q_n/2), hsum += h, with
+//      mixed-precision FMAs (bf16 / f16 products exact, fp32 sums); the group folds in as
+//      out[n] += g * (2*s[n]*(acc[n] - 8*hsum) + b[n]*hsum) -- the reference's affine algebra
+//      s * sum(h q) + b * sum(h).
 // Then the 16 group lanes are reduced in shared memory in a fixed order, and each CTA pushes
 // the 8 slices of its partial chunk to their owner CTAs with st.async (completing on the
 // owner's mbarrier); each owner sums its slice's 8 partials in rank order.
@@ -293,6 +295,23 @@ __device__ __forceinline__ void consume_rows(const uint32_t* stage, int t0, int 
   }
 }
 
+// The same, with every entry's word and h read from shared memory first and the FMAs run back
+// to back (more registers: the one-CTA-per-SM form); chs holds the raw h of list entry e at e.
+template <typename HT, int RG, int NWC>
+__device__ __forceinline__ void consume_rows_preloaded(const uint32_t* stage, const uint32_t* chs, int t0, int n,
+                                                       int lane, float (&acc)[8], float& hsum) {
+  uint32_t w[RG], hv[RG];
+#pragma unroll
+  for (int t = 0; t < RG; ++t)
+    if (t0 + t < n) {                             // warp-uniform
+      w[t] = stage[t * NWC + lane];
+      hv[t] = chs[t0 + t];
+    }
+#pragma unroll
+  for (int t = 0; t < RG; ++t)
+    if (t0 + t < n) RowMath<HT>::row(acc, hsum, hv[t], w[t]);
+}
+
 template <typename HT, typename ST, typename YT, int C, int RG, int MINB>
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MINB)
     sparse_down_decode_kernel(const DecodeParams p) {
@@ -459,13 +478,19 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kNGL * 32, MI
       float acc[8], hsum = 0.f;
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-      consume_rows<HT, RG, NWC>(&S.stage[warp][i][0][0], 0, n[i], hv0[i], hv1[i], lane, acc, hsum);
+      if constexpr (MINB == 1)
+        consume_rows_preloaded<HT, RG, NWC>(&S.stage[warp][i][0][0], &S.ch[warp][i][0], 0, n[i], lane, acc, hsum);
+      else
+        consume_rows<HT, RG, NWC>(&S.stage[warp][i][0][0], 0, n[i], hv0[i], hv1[i], lane, acc, hsum);
       for (int t0 = RG; t0 < n[i]; t0 += RG) {     // groups with more than RG live rows
         __syncwarp();
         stage_rows<RG, NWC>(smem_u32(&S.stage[warp][i][0][0]), rows[i], t0, n[i], off0[i], off1[i], nwc, lane, pol);
         cp_commit_wait();
         __syncwarp();
-        consume_rows<HT, RG, NWC>(&S.stage[warp][i][0][0], t0, n[i], hv0[i], hv1[i], lane, acc, hsum);
+        if constexpr (MINB == 1)
+          consume_rows_preloaded<HT, RG, NWC>(&S.stage[warp][i][0][0], &S.ch[warp][i][0], t0, n[i], lane, acc, hsum);
+        else
+          consume_rows<HT, RG, NWC>(&S.stage[warp][i][0][0], t0, n[i], hv0[i], hv1[i], lane, acc, hsum);
       }
       if (!meta_in) {                            // the chunks are needed from the first fold on
         if (!mbar_wait_bounded(wbar, wphase)) {
