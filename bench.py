@@ -383,6 +383,52 @@ def cpu_steps(host, ins, steps, warmup=1, budget_s=None):
     return nbytes / dt / 1e9, 1e3 * dt / n, cores, n
 
 
+def control_leg(layers, device, dist_on, steps=50, warmup=5):
+    """The reference decode bench's control (bench/decode_layers.py:14-16,163-168) at config 1
+    (B = 1, z = 0.90, the headline's inputs, 23 layers in CUDA graphs over the 8 rotating input
+    sets): the same sparse kernel and launch fed those inputs with every h element raised to at
+    least 1e-3 -- nothing to skip -- which separates "a faster kernel" from "bytes not read"; and
+    the stock dense kernel on the checkpoint layout (hsd_dense_down_decode: mlx-lm's gather_qmm
+    down projection, the reference's dense path) on the headline inputs. The checkpoint layout is
+    rebuilt from the neuron-major one (both transposes are their own inverses).
+    -> per form: us per layer, MB read per layer (the byte model), GB/s."""
+    hsd_b200 = _hsd()
+    from hsd_b200.decode import dense_down as stock
+    out = {}
+    wl = DecodeWorkload(layers, 1, 0.90, device, seed=7)
+    for _, views in wl.sets:
+        for h, _, _ in views:
+            h.clamp_(min=1e-3)
+    nb = [sum(needed_bytes(h, sel) for (h, sel, _) in views) for (_, views) in wl.sets]
+    dense_bytes = sum(nb) / len(nb)
+    wl.capture()
+    ms = timed(wl.step, steps, warmup, device, dist_on, label="hsd_control")
+    out["sparse_kernel_h_without_zeros"] = {"us_per_layer": 1e3 * ms / steps / N_LAYERS,
+                                            "MB_per_layer": dense_bytes / N_LAYERS / 1e6,
+                                            "GBps": dense_bytes * steps / (ms / 1e3) / 1e9}
+    del wl
+    ck = [hsd_b200.to_neuron_major(pw, ps, pb) + hsd_b200.to_neuron_major(spw, sps, spb)
+          for (pw, ps, pb, spw, sps, spb) in layers]
+    wl = DecodeWorkload(layers, 1, 0.90, device, seed=7)
+    wsp = torch.empty((1, TOPK + 1, D), dtype=torch.float32, device=device)
+
+    def run_stock(si, wl=wl):
+        _, views = wl.sets[si]
+        for l, (h, sel, gains) in enumerate(views):
+            stock(h, sel, gains, *ck[l], F=F, FS=FS, D=D, topk=TOPK, out=wl.ys[si][l], workspace=wsp)
+
+    wl.run_set = run_stock
+    wl.capture()
+    ms = timed(wl.step, steps, warmup, device, dist_on, label="hsd_control")
+    out["stock_dense_checkpoint_layout"] = {"us_per_layer": 1e3 * ms / steps / N_LAYERS,
+                                            "MB_per_layer": dense_bytes / N_LAYERS / 1e6,
+                                            "GBps": dense_bytes * steps / (ms / 1e3) / 1e9}
+    del wl, ck
+    out["note"] = ("bytes: every row of the 7 experts a token selects, their scales / biases, h and y (the byte "
+                   "model of the headline with every row live); the headline reads ~4.5 MB per layer")
+    return out
+
+
 def prefill_leg(layers, device, dist_on, reps=10, T=2048, chunk=512, dead_groups=0):
     """Config 2: T tokens in chunks of `chunk` through one MoE layer (layer 0), Zipf(1.1)
     routing, h = relu(N(-1.28, 1))^2. Times tile order + gather + tcgen05 GEMM + reduce per
@@ -829,6 +875,10 @@ def main():
                               "GBps": w2.bytes_per_step * k / (m2 / 1e3) / 1e9})
                 del w2
 
+    control = None
+    if not args.no_sweep and world == 1:
+        control = control_leg(layers, device, dist_on)
+
     prefill = None
     if not args.no_prefill:
         prefill = {"chunk512": prefill_leg(layers, device, dist_on),
@@ -875,6 +925,7 @@ def main():
         "clocks": clk.summary(),
         "us_per_layer": launch_ms * 1e3,
         "sweep": sweep,
+        "control": control,
         "prefill": prefill,
         "expert_parallel": ep,
         "mamba": mamba,
