@@ -26,7 +26,9 @@
 //      live rows' chunks (8 lanes a row, 16 bytes a lane, four rows per instruction: the
 //      memory system charges per request, not per byte), then the TMA bulk copies of the
 //      live groups' scale / bias chunks on the warp's mbarrier -- one more round trip (a group
-//      with more than RG live rows takes further ones);
+//      with more than RG live rows takes further ones: RG = 32 in the one-CTA-per-SM form used
+//      at B = 1, 12 in the two-CTA-per-SM form of batches, where the group lanes' partial-chunk
+//      buffer shares the staging memory);
 //   3. each group's staged words and h values are read into registers, then its rows are
 //      accumulated in ascending order: acc[n] += h * (8 + q_n/2), hsum += h, with
 //      mixed-precision FMAs (bf16 / f16 products exact, fp32 sums); the group folds in as
@@ -82,11 +84,13 @@ struct DecodeParams {
 // Shared memory of one CTA (dynamic, possibly padded by the host to limit CTAs per SM).
 template <int C, int RG>
 struct DecodeSmem {
-  uint32_t stage[kNGL][2][RG][C / 8];           // per warp and group of a round: staged live rows
+  union {
+    uint32_t stage[kNGL][2][RG][C / 8];         // per warp and group of a round: staged live rows
+    float red[kNGL][C];                         // after the rounds: the group lanes' partial chunks
+  };
   uint16_t meta[kNGL][2][2][C];                 // per warp and group of a round: scale, bias chunks
   uint32_t ch[kNGL][2][64];                     // per warp and group: h (raw bits) of the compacted live rows
   short cj[kNGL][2][64];                        //   ... and their rows
-  float red[kNGL][C];                           // the group lanes' partial chunks
   float recv[C];                                // [rank][C/8]: the slices pushed to this CTA
   uint32_t hs[2 * kNGL][64];                    // the round's h values (raw; 64 entries of up to 4 bytes)
   int64_t grow[2 * kNGL];                       // the round's groups' first neuron rows
@@ -296,20 +300,26 @@ __device__ __forceinline__ void consume_rows(const uint32_t* stage, int t0, int 
 }
 
 // The same, with every entry's word and h read from shared memory first and the FMAs run back
-// to back (more registers: the one-CTA-per-SM form); chs holds the raw h of list entry e at e.
+// to back, 16 rows at a time (more registers: the one-CTA-per-SM form); chs holds the raw h of
+// list entry e at e.
 template <typename HT, int RG, int NWC>
 __device__ __forceinline__ void consume_rows_preloaded(const uint32_t* stage, const uint32_t* chs, int t0, int n,
                                                        int lane, float (&acc)[8], float& hsum) {
-  uint32_t w[RG], hv[RG];
+  constexpr int CH = RG < 16 ? RG : 16;           // rows read into registers at a time
 #pragma unroll
-  for (int t = 0; t < RG; ++t)
-    if (t0 + t < n) {                             // warp-uniform
-      w[t] = stage[t * NWC + lane];
-      hv[t] = chs[t0 + t];
-    }
+  for (int tb = 0; tb < RG; tb += CH) {
+    if (t0 + tb >= n) break;                      // warp-uniform
+    uint32_t w[CH], hv[CH];
 #pragma unroll
-  for (int t = 0; t < RG; ++t)
-    if (t0 + t < n) RowMath<HT>::row(acc, hsum, hv[t], w[t]);
+    for (int t = 0; t < CH; ++t)
+      if (tb + t < RG && t0 + tb + t < n) {       // warp-uniform; only the rows staged this round
+        w[t] = stage[(tb + t) * NWC + lane];
+        hv[t] = chs[t0 + tb + t];
+      }
+#pragma unroll
+    for (int t = 0; t < CH; ++t)
+      if (tb + t < RG && t0 + tb + t < n) RowMath<HT>::row(acc, hsum, hv[t], w[t]);
+  }
 }
 
 template <typename HT, typename ST, typename YT, int C, int RG, int MINB>
@@ -673,8 +683,8 @@ template <typename HT, typename ST, typename YT, int C>
 int dispatch_rg(const DecodeParams& p, cudaStream_t st) {
   static const int forced = env_int("HSD_DECODE_RG");
   const int rg = (forced == 8 || forced == 16) ? forced : (p.B == 1 ? 16 : 8);
-  if (rg == 16) return launch_decode<HT, ST, YT, C, 16, 1>(p, st);
-  return launch_decode<HT, ST, YT, C, 8, 2>(p, st);
+  if (rg == 16) return launch_decode<HT, ST, YT, C, 32, 1>(p, st);
+  return launch_decode<HT, ST, YT, C, 12, 2>(p, st);
 }
 
 template <typename HT, typename ST, typename YT>

@@ -217,7 +217,8 @@ torch.save(y.cpu(), sys.argv[2])
 
 @pytest.mark.gpu
 def test_launch_shape_does_not_change_bits(cuda, tmp_path):
-    """The live rows loaded per round trip (HSD_DECODE_RG: 16 for one token, 8 for a batch)
+    """The live rows loaded per round trip (HSD_DECODE_RG: 16 selects the one-CTA-per-SM form,
+    staging 32 rows of a group per round trip, 8 the two-CTA form of batches, staging 12)
     and the CTAs per SM (shared memory padded through HSD_DECODE_SMEM) change how the work is
     scheduled, never the arithmetic (the variables are read once per process): the same bits
     on a case with ~32 live rows per group (every group takes several round trips)."""
