@@ -126,7 +126,8 @@ int hsd_decode_live_rows(const void* h, int h_dtype, int32_t* live, int32_t* cou
 /* ---- prefill: hsd/prefill.py --------------------------------------------------- */
 
 /* The fixed tile count of build_tiles (hsd/prefill.py:266,275): nt_routed =
- * T*topk/tt + E (+1 when E < tt), nt_shared = ceil(T/tt). Host-only, no device work. */
+ * T*topk/tt + E (a bound that every routing meets), nt_shared = ceil(T/tt). Host-only, no
+ * device work. */
 int hsd_prefill_num_tiles(int T, int topk, int E, int tt, int* nt_routed, int* nt_shared);
 
 /* hsd/prefill.py:247 build_tiles(sel, E, tt):

@@ -222,9 +222,10 @@ namespace hsd {
 int prefill_tile_counts(int T, int topk, int E, int tt, int* nt_routed, int* nt_shared) {
   if (T < 1 || topk < 1 || E < 1 || tt < 1)
     return set_error(HSD_ERR_SHAPE, "prefill tiles: need T, topk, E, tt >= 1");
-  // the reference's fixed bound T*topk//tt + E (hsd/prefill.py:266), which holds when
-  // E >= tt; one tile more covers E < tt
-  long long r = static_cast<long long>(T) * topk / tt + E + (E < tt ? 1 : 0);
+  // the reference's fixed bound T*topk//tt + E (hsd/prefill.py:266). It always holds: with
+  // T*topk = q*tt + r (r < tt), sum_e ceil(c_e/tt) <= (q*tt + r + E*(tt-1))/tt
+  // = q + E + (r - E)/tt < q + E + 1.
+  long long r = static_cast<long long>(T) * topk / tt + E;
   long long s = (static_cast<long long>(T) + tt - 1) / tt;
   if (r + s > (1ll << 28)) return set_error(HSD_ERR_SHAPE, "prefill tiles: too many tiles");
   *nt_routed = static_cast<int>(r);

@@ -3,7 +3,7 @@
 build_tiles   restates hsd/prefill.py:247-278: slots t*topk + k sorted by expert (stable:
               ascending slot inside an expert), tiles of tt slots of one expert at
               tile_base[e] = sum of earlier experts' ceil(count / tt), a fixed routed tile
-              count T*topk//tt + E (+1 when E < tt), -1 for empty tiles and padding, then the
+              count T*topk//tt + E, -1 for empty tiles and padding, then the
               shared expert's ceil(T/tt) tiles of tokens (expert id E).
 build_union   restates hsd/prefill.py:48-93,281-291: per tile the ascending columns nonzero
               in any slot, -1 padded to umax.
@@ -16,7 +16,7 @@ from .decode import reference_dense
 
 
 def num_tiles(T, topk, E, tt):
-    return T * topk // tt + E + (1 if E < tt else 0), (T + tt - 1) // tt
+    return T * topk // tt + E, (T + tt - 1) // tt
 
 
 def build_tiles(sel, E, tt):

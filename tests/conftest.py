@@ -48,3 +48,31 @@ def rel_err(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+# ---- fixtures produced by the reference's own code (tests/golden/make_reference_golden.py)
+
+REF_HASHED_SHAPES = ((2688, 232), (1856, 336), (3712, 336), (3, 2688, 232))
+
+
+def reference_words(shape):
+    """The seeded words whose reference transpose is pinned by sha256 in reference_layout.npz
+    (the same rule as the generator: default_rng(prod(shape) mod 2^31))."""
+    rng = np.random.default_rng(int(np.prod(shape)) % (2**31))
+    return rng.integers(0, 2**32, size=shape, dtype=np.uint64).astype(np.uint32)
+
+
+def sha256_np(a):
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def reference_tile_cases():
+    """(name, sel, E, tt, tile_e, tile_slot) of every case in reference_tiles.npz."""
+    g = np.load(os.path.join(GOLDEN, "reference_tiles.npz"))
+    names = sorted(k[:-len("_dims")] for k in g.files if k.endswith("_dims"))
+    out = []
+    for n in names:
+        T, topk, E, tt = (int(v) for v in g[n + "_dims"])
+        out.append((n, g[n + "_sel"], E, tt, g[n + "_tile_e"], g[n + "_tile_slot"]))
+    return out

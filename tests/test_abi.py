@@ -92,7 +92,7 @@ def test_ep_buffer_sizes_and_argument_checks():
     assert _rc("hsd_ep_buffer_bytes", 8, 512, 6, 1856, 3712, 2688, 128, 0, ctypes.byref(ib), ctypes.byref(wb)) == L.HSD_OK
     # inbox: 8 ranks x 3072 slots of h rows + ids, gains, return addresses, + 3072 + 512 fp32 partial rows
     assert 130e6 < ib.value < 131e6
-    assert 202e6 < wb.value < 204e6         # dominated by the gathered fp16 A tiles (K up to FS)
+    assert 201e6 < wb.value < 203e6         # dominated by the gathered fp16 A tiles (K up to FS)
     one_i, one_w = ctypes.c_size_t(0), ctypes.c_size_t(0)
     assert _rc("hsd_ep_buffer_bytes", 1, 512, 6, 1856, 3712, 2688, 128, 0, ctypes.byref(one_i), ctypes.byref(one_w)) == 0
     assert one_i.value < ib.value

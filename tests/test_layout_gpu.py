@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN, bits16_np, words_np
+from conftest import GOLDEN, REF_HASHED_SHAPES, bits16_np, reference_words, sha256_np, words_np
 from oracle import layout as ol
 
 import hsd_b200
@@ -64,3 +64,33 @@ def test_swap_last2_f16_and_odd_sizes(cuda):
     y = hsd_b200.swap_last2(x)
     assert torch.equal(y, x.transpose(-1, -2).contiguous())
     assert np.array_equal(bits16_np(y), np.swapaxes(bits16_np(x), -1, -2))
+
+
+def _u16(a, dev):
+    return torch.from_numpy(a.view(np.int16)).to(dev).view(torch.bfloat16)
+
+
+@pytest.mark.gpu
+def test_layout_matches_reference_code(cuda):
+    """The CUDA permutation against outputs of the reference's own hsd/layout.py:34-74 (run
+    through a numpy stand-in of mlx.core): two small shapes, a 20-expert stack (more than the
+    16-expert chunk) and a 2-D shared expert, words and bf16 scale / bias bits bit-exact."""
+    g = np.load(os.path.join(GOLDEN, "reference_layout.npz"))
+    for key in ("5x24x9", "2x16x4"):
+        t = hsd_b200.nibble_transpose(torch.from_numpy(g["nt_w_" + key].view(np.int32)).to(cuda))
+        assert np.array_equal(words_np(t), g["nt_t_" + key])
+    for pre in ("ntm_", "ntm_s"):
+        w = torch.from_numpy(g[pre + "w"].view(np.int32)).to(cuda)
+        pw, ps, pb = hsd_b200.to_neuron_major(w, _u16(g[pre + "s"], cuda), _u16(g[pre + "b"], cuda))
+        assert np.array_equal(words_np(pw), g[pre + "pw"])
+        assert np.array_equal(bits16_np(ps), g[pre + "ps"]) and np.array_equal(bits16_np(pb), g[pre + "pb"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", REF_HASHED_SHAPES)
+def test_nibble_transpose_reference_hash(cuda, shape):
+    """The reference test's larger shapes: sha256 of the CUDA transpose of the seeded words ==
+    sha256 of the reference code's own transpose of the same words."""
+    g = np.load(os.path.join(GOLDEN, "reference_layout.npz"))
+    t = hsd_b200.nibble_transpose(torch.from_numpy(reference_words(shape).view(np.int32)).to(cuda))
+    assert sha256_np(words_np(t)) == str(g["nt_sha_" + "x".join(map(str, shape))])

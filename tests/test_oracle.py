@@ -6,7 +6,8 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN, rel_err
+from conftest import (GOLDEN, REF_HASHED_SHAPES, reference_tile_cases, reference_words, rel_err,
+                      sha256_np)
 from oracle import cport
 from oracle import decode as od
 from oracle import layout as ol
@@ -49,6 +50,41 @@ def test_nibble_transpose_golden(name):
     g = np.load(os.path.join(GOLDEN, name))
     assert np.array_equal(ol.nibble_transpose(g["w"]), g["t"])
     assert np.array_equal(cport.nibble_transpose(g["w"]), g["t"])
+
+
+def test_layout_matches_reference_code():
+    """nibble_transpose / to_neuron_major against outputs of the reference's own
+    hsd/layout.py:34-74 (run through a numpy stand-in of mlx.core): two small shapes in full,
+    a 20-expert stack (the chunked branch) and a 2-D shared expert with their scale bits."""
+    g = np.load(os.path.join(GOLDEN, "reference_layout.npz"))
+    for key in ("5x24x9", "2x16x4"):
+        assert np.array_equal(ol.nibble_transpose(g["nt_w_" + key]), g["nt_t_" + key])
+        assert np.array_equal(cport.nibble_transpose(g["nt_w_" + key]), g["nt_t_" + key])
+    for pre in ("ntm_", "ntm_s"):                    # keys ntm_{w,s,b,pw,ps,pb}, ntm_s{...}
+        out = ol.to_neuron_major(g[pre + "w"], g[pre + "s"], g[pre + "b"])
+        for got, name in zip(out, ("pw", "ps", "pb")):
+            assert np.array_equal(got, g[pre + name]), (pre, name)
+
+
+@pytest.mark.parametrize("shape", REF_HASHED_SHAPES)
+def test_nibble_transpose_reference_hash(shape):
+    """The reference test's larger shapes: the oracle's transpose of the seeded words hashes to
+    the sha256 of the reference code's own transpose of the same words."""
+    g = np.load(os.path.join(GOLDEN, "reference_layout.npz"))
+    t = ol.nibble_transpose(reference_words(shape))
+    assert sha256_np(t) == str(g["nt_sha_" + "x".join(map(str, shape))])
+
+
+@pytest.mark.parametrize("case", reference_tile_cases(), ids=lambda c: c[0])
+def test_build_tiles_matches_reference_code(case):
+    """build_tiles against the reference's own hsd/prefill.py:247-278 on seeded routings:
+    uniform, Zipf-skewed, every slot on one expert, one token, E < tt and E >= tt."""
+    from oracle import prefill as op
+    name, sel, E, tt, te_ref, ts_ref = case
+    te, ts = op.build_tiles(sel, E, tt)
+    assert np.array_equal(te, te_ref) and np.array_equal(ts, ts_ref)
+    T, K = sel.shape
+    assert sum(op.num_tiles(T, K, E, tt)) == te_ref.shape[0]
 
 
 def test_c_transpose_matches_numpy():

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import bits16_np, f32_np, rel_err, words_np
+from conftest import bits16_np, f32_np, reference_tile_cases, rel_err, words_np
 from oracle import cport
 from oracle import prefill as op
 
@@ -38,6 +38,17 @@ def test_build_tiles_bit_exact(cuda, T, E, topk, tt):
     ote, ots = op.build_tiles(sel.cpu().numpy(), E, tt)
     assert np.array_equal(te.cpu().numpy(), ote)
     assert np.array_equal(ts.cpu().numpy(), ots)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", reference_tile_cases(), ids=lambda c: c[0])
+def test_build_tiles_matches_reference_code(cuda, case):
+    """The CUDA tile order against outputs of the reference's own hsd/prefill.py:247-278 (run
+    through a numpy stand-in of mlx.core), same tile count, bit-exact."""
+    name, sel, E, tt, te_ref, ts_ref = case
+    te, ts = hp.build_tiles(torch.from_numpy(sel).to(cuda), E, tt)
+    assert np.array_equal(te.cpu().numpy(), te_ref)
+    assert np.array_equal(ts.cpu().numpy(), ts_ref)
 
 
 @pytest.mark.gpu
