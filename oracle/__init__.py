@@ -13,9 +13,11 @@ Pinning (what each part was checked against):
            tests/test_oracle.py (exactness, self-inverse, the reference test's shapes).
   decode   the reference test's fp32 dequantised reference (tests/test_layout_decode.py
            :128-142) and, independently, the Metal kernel's per-group affine algebra
-           (hsd/decode.py:105-144); the two restatements must agree. No output of the
-           reference itself exists offline (MLX needs Apple silicon), so the decode
-           oracle is pinned by algebra only.
+           (hsd/decode.py:105-144); the two restatements must agree. That test reference
+           itself, run unmodified on the numpy stand-in of mlx.core, produced
+           tests/golden/reference_down.npz; the oracle reproduces it to 1e-5 once the
+           dequantised weights are rounded to bf16 as mx.dequantize returns them. The
+           Metal kernels' own outputs do not exist offline (MLX needs Apple silicon).
   prefill  tile order: outputs of the reference's own hsd/prefill.py:247-278 on seeded
            routings, run the same way (tests/golden/reference_tiles.npz); union, gain
            epilogue and partial sum restated from hsd/prefill.py:48-222,281-321 (Metal).

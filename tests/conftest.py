@@ -76,3 +76,10 @@ def reference_tile_cases():
         T, topk, E, tt = (int(v) for v in g[n + "_dims"])
         out.append((n, g[n + "_sel"], E, tt, g[n + "_tile_e"], g[n + "_tile_slot"]))
     return out
+
+
+def reference_down_case():
+    """reference_down.npz: (dims dict, arrays) -- y from the reference test's reference()."""
+    g = np.load(os.path.join(GOLDEN, "reference_down.npz"))
+    D, F, FS, E, topk, B = (int(x) for x in g["dims"])
+    return dict(D=D, F=F, FS=FS, E=E, topk=topk, B=B), g

@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN, bits16_np, f32_np, rel_err, words_np
+from conftest import GOLDEN, bits16_np, f32_np, reference_down_case, rel_err, words_np
 from oracle import cport
 from oracle import decode as od
 from oracle.quant import bf16_bits_to_f32
@@ -48,6 +48,37 @@ def test_golden_small_case(cuda):
     y = hsd_b200.sparse_down(h, t(g["sel"], np.int32), t(g["gains"], np.float32), *args, F=F, FS=FS, D=D,
                              topk=topk, out_dtype=torch.float32)
     assert rel_err(f32_np(y), g["y"]) < TOL
+    assert hsd_b200.device_status() == 0
+
+
+def _reference_down_inputs(cuda):
+    dims, g = reference_down_case()
+    t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).view(dt)).to(cuda)  # noqa: E731
+    bf = lambda a: t(a, np.int16).view(torch.bfloat16)  # noqa: E731
+    ck = (t(g["w"], np.int32), bf(g["s"]), bf(g["b"]), t(g["sw"], np.int32), bf(g["ss"]), bf(g["sb"]))
+    return dims, g, bf(g["h"]), t(g["sel"], np.int32), t(g["gains"], np.float32), ck
+
+
+@pytest.mark.gpu
+def test_matches_reference_code_fp32_reference(cuda):
+    """Sparse and dense forms on the neuron-major layout, and the stock checkpoint-layout kernel,
+    against y of the reference test's own fp32 reference (tests/test_layout_decode.py:128-142,
+    run unmodified on a numpy stand-in of mlx.core; its bf16-rounded dequantised weights are
+    the whole difference), within the reference test's bound 2e-3; each token alone equals its
+    row of the batch bit for bit."""
+    dims, g, h, sel, gains, ck = _reference_down_inputs(cuda)
+    kw = dict(F=dims["F"], FS=dims["FS"], D=dims["D"], topk=dims["topk"], out_dtype=torch.float32)
+    lay = hsd_b200.to_neuron_major(*ck[:3]) + hsd_b200.to_neuron_major(*ck[3:])
+    y = hsd_b200.sparse_down(h, sel, gains, *lay, **kw)
+    assert rel_err(f32_np(y), g["y"]) < TOL
+    yd = hsd_b200.sparse_down(h, sel, gains, *lay, all_rows=True, **kw)
+    assert torch.equal(y, yd)
+    from hsd_b200.decode import dense_down
+    ys = dense_down(h, sel, gains, *ck, **kw)
+    assert rel_err(f32_np(ys), g["y"]) < TOL
+    for b in range(dims["B"]):
+        y1 = hsd_b200.sparse_down(h[b:b + 1], sel[b:b + 1], gains[b:b + 1], *lay, **kw)
+        assert torch.equal(y1[0], y[b])
     assert hsd_b200.device_status() == 0
 
 

@@ -6,8 +6,8 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import (GOLDEN, REF_HASHED_SHAPES, reference_tile_cases, reference_words, rel_err,
-                      sha256_np)
+from conftest import (GOLDEN, REF_HASHED_SHAPES, reference_down_case, reference_tile_cases, reference_words,
+                      rel_err, sha256_np)
 from oracle import cport
 from oracle import decode as od
 from oracle import layout as ol
@@ -85,6 +85,34 @@ def test_build_tiles_matches_reference_code(case):
     assert np.array_equal(te, te_ref) and np.array_equal(ts, ts_ref)
     T, K = sel.shape
     assert sum(op.num_tiles(T, K, E, tt)) == te_ref.shape[0]
+
+
+def test_down_projection_matches_reference_code():
+    """The oracle against y of the reference test's own fp32 reference (tests/test_layout_decode.py
+    :128-142 of the reference, run unmodified on a numpy stand-in of mlx.core): within the
+    reference test's bound 2e-3 of max|ref| with the unrounded weights s*q + b (what the
+    kernels use), and within 1e-5 once the dequantised weights are rounded to bf16 the way
+    the stand-in's mx.dequantize returns them -- so the two differ by that rounding alone."""
+    dims, g = reference_down_case()
+    F, FS, topk = dims["F"], dims["FS"], dims["topk"]
+    f = bf16_bits_to_f32
+    hf = f(g["h"])
+    y = od.reference_dense(hf, g["sel"], g["gains"], g["w"], f(g["s"]), f(g["b"]), g["sw"], f(g["ss"]),
+                           f(g["sb"]), F=F, FS=FS, topk=topk)
+    assert rel_err(y, g["y"]) < 2e-3
+
+    def bf16(x):
+        u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32).view(np.float32)
+
+    Wd = bf16(dequantize(g["w"], f(g["s"]), f(g["b"])))           # [E, D, F]
+    Ws = bf16(dequantize(g["sw"], f(g["ss"]), f(g["sb"])))          # [D, FS]
+    yr = np.zeros_like(y, dtype=np.float64)
+    for t in range(dims["B"]):
+        for k in range(topk):
+            yr[t] += g["gains"][t, k] * (Wd[g["sel"][t, k]].astype(np.float64) @ hf[t, k * F:(k + 1) * F])
+        yr[t] += Ws.astype(np.float64) @ hf[t, topk * F:]
+    assert rel_err(yr, g["y"]) < 1e-5
 
 
 def test_c_transpose_matches_numpy():

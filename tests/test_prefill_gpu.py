@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import bits16_np, f32_np, reference_tile_cases, rel_err, words_np
+from conftest import bits16_np, f32_np, reference_down_case, reference_tile_cases, rel_err, words_np
 from oracle import cport
 from oracle import prefill as op
 
@@ -49,6 +49,23 @@ def test_build_tiles_matches_reference_code(cuda, case):
     te, ts = hp.build_tiles(torch.from_numpy(sel).to(cuda), E, tt)
     assert np.array_equal(te.cpu().numpy(), te_ref)
     assert np.array_equal(ts.cpu().numpy(), ts_ref)
+
+
+@pytest.mark.gpu
+def test_prefill_matches_reference_code_fp32_reference(cuda):
+    """The prefill path against y of the reference test's own fp32 reference
+    (tests/test_layout_decode.py:128-142, run unmodified on a numpy stand-in of mlx.core),
+    within the reference's prefill bound."""
+    dims, g = reference_down_case()
+    t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).view(dt)).to(cuda)  # noqa: E731
+    bf = lambda a: t(a, np.int16).view(torch.bfloat16)  # noqa: E731
+    lay = hsd_b200.to_neuron_major(t(g["w"], np.int32), bf(g["s"]), bf(g["b"])) + \
+        hsd_b200.to_neuron_major(t(g["sw"], np.int32), bf(g["ss"]), bf(g["sb"]))
+    y = hsd_b200.sparse_down_prefill(bf(g["h"]), t(g["sel"], np.int32), t(g["gains"], np.float32), *lay,
+                                     F=dims["F"], FS=dims["FS"], D=dims["D"], topk=dims["topk"], E=dims["E"],
+                                     out_dtype=torch.float32)
+    assert rel_err(f32_np(y), g["y"]) < TOL
+    assert hsd_b200.device_status() == 0
 
 
 @pytest.mark.gpu
