@@ -218,6 +218,32 @@ def test_prefill_tiles_oracle_properties():
     assert sorted(sh[sh >= 0].tolist()) == list(range(T))
 
 
+@pytest.mark.parametrize("T,topk,E,tt", [(300, 2, 8, 128), (37, 3, 8, 4), (1, 6, 128, 128), (100, 6, 16, 32),
+                                           (129, 1, 2, 128), (4096, 6, 128, 128), (1000, 6, 100, 128)])
+def test_routed_tile_bound_is_tight_and_holds(T, topk, E, tt):
+    """The reference's fixed routed tile count T*topk//tt + E (hsd/prefill.py:266) is an upper
+    bound for every routing: with T*topk = q*tt + r, the tiles needed are at most
+    q + E + (r - E)/tt < q + E + 1. Checked on the routing that needs the most tiles -- one
+    slot on each of E - 1 experts and the rest on one (tight when r >= E) -- and on a
+    uniform one: every slot is placed."""
+    from oracle import prefill as op
+    N = T * topk
+    flat = np.full(N, E - 1, np.int32)
+    flat[:min(E - 1, N)] = np.arange(min(E - 1, N))
+    rng = np.random.default_rng(T + E)
+    for sel in (flat.reshape(T, topk), rng.integers(0, E, size=(T, topk)).astype(np.int32)):
+        counts = np.bincount(sel.reshape(-1), minlength=E)
+        need = int(((counts + tt - 1) // tt).sum())
+        nr, ns = op.num_tiles(T, topk, E, tt)
+        assert need <= nr == N // tt + E
+        te, ts = op.build_tiles(sel, E, tt)
+        routed = ts[:nr * tt]
+        assert sorted(routed[routed >= 0].tolist()) == list(range(N))
+    r = N % tt
+    if r >= E:
+        assert int(((np.bincount(flat, minlength=E) + tt - 1) // tt).sum()) == nr
+
+
 def test_prefill_union_oracle_small():
     from oracle import prefill as op
     h = np.zeros((2, 2 * 64 + 64), np.float32)
