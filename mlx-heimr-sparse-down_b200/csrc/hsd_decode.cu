@@ -640,10 +640,11 @@ __global__ void __launch_bounds__(kLiveThreads) live_rows_kernel(const void* h, 
 
 // Launch shape. Chunks of C = 256 outputs (a chunk row is one warp's 32 words; at D = 2688
 // a token is 10 full chunks and a half-width tail, 88 CTAs per token) and 16 warps per CTA.
-// One token loads up to 16 live rows of a group per round trip (112 registers, one CTA per
-// SM); a batch up to 8 (64 registers: two CTAs per SM, so a 3-row verify step runs in one
-// wave). HSD_DECODE_RG (8, 16) and HSD_DECODE_SMEM (dynamic shared memory in bytes, to limit
-// the CTAs per SM) override the choice; HSD_DECODE_CHUNK (128, 192, 256) the chunk width.
+// One token loads up to 32 live rows of a group per round trip (128 registers, one CTA per
+// SM); a batch up to 12 (64 registers: two CTAs per SM, so a 3-row verify step runs in one
+// wave). HSD_DECODE_RG (16: the one-token form, 8: the batch form) and HSD_DECODE_SMEM
+// (dynamic shared memory in bytes, to limit the CTAs per SM) override the choice;
+// HSD_DECODE_CHUNK (128, 160, 192, 256) the chunk width.
 // None of them changes a token's arithmetic.
 int env_int(const char* name) {
   const char* e = getenv(name);
